@@ -1,0 +1,401 @@
+#!/usr/bin/env python
+"""Benchmark of the fused NF4 / fp8 weight-only linear on B200.
+
+One step = one fused quantized linear over one batch of synthetic tokens:
+x bf16 [4608, 3072] (one 1024x1024 FLUX image's 4096 latent + 512 text
+tokens) times W [12288, 3072] (NF4 by default, the FLUX feed-forward up
+projection shape), y bf16 [4608, 12288].  With N GPUs (torchrun, one process
+per GPU) every rank runs its own token batch against a replicated weight: data
+parallel, no data-path collective, weak scaling; the value is the whole-job
+TFLOP/s from the max-over-ranks device time.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload nf4|fp8]
+    python bench.py --impl reference ...   # the reference's CPU algorithm
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import datetime
+import json
+import os
+import re
+import statistics
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M, N, K = 4608, 12288, 3072
+FLOPS_PER_STEP = 2 * M * N * K
+ROTATE = 4  # rotating input sets: 4 x (x + W + y) = 650 MB > 126 MB L2
+REF_ROW_SLICE = 16  # the CPU reference arm times 1/16 of the weight rows per step
+
+WORKLOADS = {
+    "nf4": {
+        "desc": "nf4_linear x[4608,3072]bf16 . W[12288,3072]nf4^T (+f32 absmax per 64) -> y[4608,12288]bf16",
+        "bytes": M * K * 2 + N * K // 2 + N * K // 64 * 4 + M * N * 2,
+    },
+    "fp8": {
+        "desc": "fp8_linear x[4608,3072]bf16 . W[12288,3072]e4m3^T (per-tensor scale) -> y[4608,12288]bf16",
+        "bytes": M * K * 2 + N * K + 4 + M * N * 2,
+    },
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="nf4")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------- peaks
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 1590.0, 6650.0, "fallback"
+
+
+def profile_traffic(workload: str):
+    """DRAM bytes per launch of the fused kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", f"dq_gemm_{workload}_4608x3072x12288.md")
+    try:
+        txt = open(path).read()
+    except OSError:
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", txt)
+    return float(m.group(1)) if m else None
+
+
+# ------------------------------------------------------------------ clocks
+REASONS = {
+    0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+    0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+    0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+}
+
+
+class ClockSampler:
+    """Polls the SM clock and clock-event reasons through NVML while running."""
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self.period = period_s
+        self._stop = threading.Event()
+        self._h = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            props = torch.cuda.get_device_properties(device_index)
+            bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+            try:
+                self._h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self._nvml = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._h = None
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _sample(self):
+        nv = self._nvml
+        self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+        self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                return
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._h is not None:
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._h is not None:
+            self._t.join()
+            try:
+                self._sample()
+            except Exception:
+                pass
+
+    def summary(self):
+        if self._h is None or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml_unavailable"]}
+        names = [v for k, v in REASONS.items() if self.reasons & k]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------- distributed
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def max_over_ranks(val: float, world: int, device) -> float:
+    if world == 1:
+        return val
+    import torch.distributed as dist
+    t = torch.tensor([val], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ----------------------------------------------------------- CPU reference
+def cpu_reference_step_fn(workload: str, row_slice: int):
+    """The reference's CPU algorithm on 1/row_slice of the weight rows, float32
+    (the reference computes in float32 on CPU): per forward, chunked byte-LUT
+    dequantization of the NF4 weight (or e4m3 upcast x scale) into a reusable
+    buffer, then torch.nn.functional.linear (R/nf4_ltx23.R:235-246,
+    R/fp8_ltx23.R:70-83).  Returns (step_fn, flops_per_step, description)."""
+    from oracle import torch_ref as T
+    n_s = N // row_slice
+    g = torch.Generator().manual_seed(0)
+    w = torch.randn(n_s, K, generator=g) * 0.02
+    x = torch.randn(M, K, generator=torch.Generator().manual_seed(1))
+    wbuf = torch.empty(n_s, K, dtype=torch.float32)
+    if workload == "nf4":
+        packed, absmax = T.ltx23_nf4_quantize(w)
+
+        def step():
+            return T.nf4_linear_forward(x, packed, absmax, n_s, K, None, w_buffer=wbuf)
+    else:
+        w8, scale = T.fp8_quantize(w)
+
+        def step():
+            return T.fp8_linear_forward(x, w8, scale, None, w_buffer=wbuf)
+    desc = (f"reference CPU op sequence (torch {torch.__version__}, float32) on x[{M},{K}] and "
+            f"1/{row_slice} of W ({n_s} of {N} rows) per step")
+    return step, 2 * M * n_s * K, desc
+
+
+def run_cpu_baseline(workload: str, budget_s: float = 12.0):
+    step, flops, desc = cpu_reference_step_fn(workload, REF_ROW_SLICE)
+    step()
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        step()
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or n >= 200:
+            break
+    return {"value": flops * n / el / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"{desc}; {n} steps in {el:.1f} s"}
+
+
+def run_reference_arm(args, world, rank):
+    if rank != 0:
+        return
+    step, flops, desc = cpu_reference_step_fn(args.workload, REF_ROW_SLICE)
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    val = flops * args.steps / el / 1e12
+    line = {
+        "metric": "NF4/fp8 quant-linear TFLOP/s", "value": val, "unit": "TFLOP/s",
+        "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOADS[args.workload]["desc"], "format": args.workload,
+                   "parallelism": "host cores of rank 0"},
+        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": desc},
+        "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(args, world, rank, local):
+    from diffuser_b200 import _lib, modules, ops
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    lib = _lib.lib()
+    stream = torch.cuda.current_stream(dev)
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+    fmt = args.workload
+
+    # Weights: one seeded fp32 W quantized on the GPU, replicated into ROTATE
+    # buffers (distinct addresses, so no launch finds its operands in L2).
+    g0 = torch.Generator(device=dev).manual_seed(0)
+    w = torch.randn(N, K, generator=g0, device=dev) * 0.02
+    if fmt == "nf4":
+        p0, a0 = ops.ltx23_nf4_quantize(w)
+        wsets = [(p0.clone(), a0.clone()) for _ in range(ROTATE)]
+        scale = 0.0
+    else:
+        w80, s0 = ops.fp8_quantize(w)
+        wsets = [(w80.view(torch.uint8).clone(), None) for _ in range(ROTATE)]
+        scale = float(s0.item())
+    del w
+    xs, ys = [], []
+    for i in range(ROTATE):
+        gx = torch.Generator(device=dev).manual_seed(1 + 100 * rank + i)
+        xs.append(torch.randn(M, K, generator=gx, device=dev).to(torch.bfloat16))
+        ys.append(torch.empty(M, N, dtype=torch.bfloat16, device=dev))
+    ws_bytes = ops.workspace_size(M, N, K, 0 if fmt == "nf4" else 1)
+    ws = ops.workspace(dev, ws_bytes)
+    wsp = ctypes.c_void_p(ws.data_ptr()) if ws is not None else None
+    launches_per_step = 1 + (1 if ws_bytes > 0 else 0)
+
+    def launch(i):
+        x, y = xs[i % ROTATE], ys[i % ROTATE]
+        wp, ap = wsets[i % ROTATE]
+        if fmt == "nf4":
+            rc = lib.dq_linear_nf4(ctypes.c_void_p(x.data_ptr()), M, K, ctypes.c_void_p(wp.data_ptr()),
+                                   ctypes.c_void_p(ap.data_ptr()), None, N, ctypes.c_void_p(y.data_ptr()),
+                                   wsp, ws_bytes, sptr)
+        else:
+            rc = lib.dq_linear_fp8(ctypes.c_void_p(x.data_ptr()), M, K, ctypes.c_void_p(wp.data_ptr()),
+                                   ctypes.c_float(scale), None, N, ctypes.c_void_p(y.data_ptr()),
+                                   wsp, ws_bytes, sptr)
+        if rc != 0:
+            raise _lib.DqError("dq_linear", rc)
+
+    for i in range(max(args.warmup, 3)):
+        launch(i)
+    torch.cuda.synchronize()
+
+    # ---- device-timed region: exactly K steps, events on the launch stream
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t_start.record(stream)
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            launch(i)
+            ev[i][1].record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    el_ms = t_start.elapsed_time(t_end)
+    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    el_ms_max = max_over_ranks(el_ms, world, dev)
+    kern_ms_max = max_over_ranks(kern_ms, world, dev)
+    err = ops.device_error(dev)
+    if err != 0:
+        raise RuntimeError(f"kernel error word {err}")
+
+    # ---- end-to-end through the public module API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        mod = modules.ltx23_nf4_linear(N, K, bias=False) if fmt == "nf4" else \
+            modules.ltx23_fp8_linear(N, K, bias=False)
+        mod = mod.to(dev)
+        if fmt == "nf4":
+            mod.set_nf4_weight(wsets[0][0], wsets[0][1])
+        else:
+            mod.set_fp8_weight(wsets[0][0].view(torch.float8_e4m3fn), torch.tensor(scale))
+        xh = [xs[i].cpu().pin_memory() for i in range(2)]
+        yh = [torch.empty(M, N, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+        xd = torch.empty(M, K, dtype=torch.bfloat16, device=dev)
+        n_e2e = max(10, min(args.steps, 200))
+
+        def e2e_step(i):
+            xd.copy_(xh[i % 2], non_blocking=True)
+            y = mod(xd)
+            yh[i % 2].copy_(y, non_blocking=True)
+
+        for i in range(3):
+            e2e_step(i)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world)
+        torch.cuda.synchronize()
+        a.record(stream)
+        for i in range(n_e2e):
+            e2e_step(i)
+        b.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        e_ms = max_over_ranks(a.elapsed_time(b), world, dev)
+        e2e = {"value": world * FLOPS_PER_STEP * n_e2e / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2,
+               "steps": n_e2e, "ms_per_step": e_ms / n_e2e,
+               "api": "diffuser_b200.modules.ltx23_%s_linear.forward" % fmt}
+
+    if rank == 0:
+        peak_tf, peak_bw, peak_src = measured_peaks()
+        achieved = FLOPS_PER_STEP / (kern_ms_max * 1e-3) / 1e12
+        traffic = profile_traffic(fmt)
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = run_cpu_baseline(fmt)
+        line = {
+            "metric": "NF4/fp8 quant-linear TFLOP/s",
+            "value": world * FLOPS_PER_STEP * args.steps / (el_ms_max * 1e-3) / 1e12,
+            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": el_ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOADS[fmt]["desc"], "format": fmt, "M": M, "N": N, "K": K,
+                       "bias": False, "parallelism": f"dp{world} (own token batch per GPU, replicated weight, no collective)",
+                       "l2": f"{ROTATE} rotating input sets ({ROTATE * WORKLOADS[fmt]['bytes'] / 1e6:.0f} MB) > 126 MB L2"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
+                         "frac": achieved / peak_tf, "traffic": traffic,
+                         "peak_source": f"{peak_src} bf16 dense (burst)",
+                         "kernel": f"dq_gemm_kernel<{fmt}>", "kernel_ms": kern_ms_max,
+                         "algorithmic_bytes": WORKLOADS[fmt]["bytes"]},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": args.steps * launches_per_step,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        run_reference_arm(args, world, rank)
+        return
+    run_ours(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    main()

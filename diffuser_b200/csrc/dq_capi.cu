@@ -1,0 +1,508 @@
+// dq_capi.cu -- C ABI of the quantized-linear engine (include/dq_linear.h):
+// argument validation, launch planning, TMA descriptors, and the standalone
+// quantize / dequantize / split-K reduce kernels.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdio>
+#include <cstdlib>
+#include <mutex>
+
+#include "../../include/dq_linear.h"
+#include "dq_gemm.cuh"
+
+#define DQ_VERSION_STRING "dqlinear-b200 0.1.0 (sm_100a)"
+
+namespace dq {
+
+// ------------------------------------------------------- standalone kernels
+// NF4 -> bf16: one thread per 16 packed bytes (32 elements of one block).
+__global__ void dequant_nf4_kernel(const uint4* __restrict__ packed, const float* __restrict__ absmax,
+                                   uint4* __restrict__ out, int64_t n_chunks) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n_chunks;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint4 p = __ldg(packed + i);
+    const uint32_t sc2 = nf4_scale2(__ldg(absmax + (i >> 1)));
+    uint32_t o[16];
+    nf4_decode_word(p.x, sc2, o + 0);
+    nf4_decode_word(p.y, sc2, o + 4);
+    nf4_decode_word(p.z, sc2, o + 8);
+    nf4_decode_word(p.w, sc2, o + 12);
+    uint4* dst = out + 4 * i;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dst[j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+  }
+}
+
+// e4m3 -> bf16: 16 bytes per thread on the aligned body, scalar tail.
+__global__ void dequant_fp8_kernel(const uint8_t* __restrict__ w8, float scale,
+                                   __nv_bfloat16* __restrict__ out, int64_t n) {
+  const float s = __bfloat162float(__float2bfloat16_rn(scale));
+  const int64_t n16 = n / 16;
+  const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const int64_t nth = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = tid; i < n16; i += nth) {
+    const uint4 p = __ldg(reinterpret_cast<const uint4*>(w8) + i);
+    uint32_t o[8];
+    fp8_decode_word(p.x, s, o + 0);
+    fp8_decode_word(p.y, s, o + 2);
+    fp8_decode_word(p.z, s, o + 4);
+    fp8_decode_word(p.w, s, o + 6);
+    uint4* dst = reinterpret_cast<uint4*>(out) + 2 * i;
+    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+  for (int64_t i = n16 * 16 + tid; i < n; i += nth) {
+    uint32_t o[2];
+    fp8_decode_word(static_cast<uint32_t>(w8[i]), s, o);
+    out[i] = __ushort_as_bfloat16(static_cast<unsigned short>(o[0] & 0xFFFFu));
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ float load_f32(const T* p, int64_t i);
+template <>
+__device__ __forceinline__ float load_f32<float>(const float* p, int64_t i) { return p[i]; }
+template <>
+__device__ __forceinline__ float load_f32<__nv_bfloat16>(const __nv_bfloat16* p, int64_t i) {
+  return __bfloat162float(p[i]);
+}
+
+// NF4 quantizer: one warp per 64-element block, two elements per lane.
+template <typename T>
+__global__ void quantize_nf4_kernel(const T* __restrict__ w, uint8_t* __restrict__ packed,
+                                    float* __restrict__ absmax, int64_t n_blocks) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t b = warp0; b < n_blocks; b += nwarps) {
+    const float v0 = load_f32(w, b * 64 + 2 * lane);
+    const float v1 = load_f32(w, b * 64 + 2 * lane + 1);
+    float a = fmaxf(fabsf(v0), fabsf(v1));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    a = fmaxf(a, 1e-12f);
+    const uint32_t c0 = nf4_code(__fdiv_rn(v0, a));
+    const uint32_t c1 = nf4_code(__fdiv_rn(v1, a));
+    packed[b * 32 + lane] = static_cast<uint8_t>((c0 << 4) | c1);
+    if (lane == 0) absmax[b] = a;
+  }
+}
+
+// fp8 quantizer, pass 1: max |w| as ordered float bits (non-negative floats
+// order like their bit patterns).
+template <typename T>
+__global__ void absmax_kernel(const T* __restrict__ w, int64_t n, unsigned int* __restrict__ amax_bits) {
+  float a = 0.f;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    a = fmaxf(a, fabsf(load_f32(w, i)));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(amax_bits, __float_as_uint(a));
+}
+
+__device__ __forceinline__ float fp8_scale_from_bits(unsigned int bits) {
+  return __fdiv_rn(fmaxf(__uint_as_float(bits), 1e-12f), 448.0f);
+}
+
+// fp8 quantizer, pass 2: w8 = e4m3(w / scale).
+template <typename T>
+__global__ void quantize_fp8_kernel(const T* __restrict__ w, int64_t n, const unsigned int* amax_bits,
+                                    uint8_t* __restrict__ w8) {
+  const float scale = fp8_scale_from_bits(*amax_bits);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    w8[i] = f32_to_e4m3(__fdiv_rn(load_f32(w, i), scale));
+}
+
+// fp8 quantizer, pass 3: replace the max bits by the scale itself.
+__global__ void finalize_fp8_scale_kernel(unsigned int* amax_bits_then_scale) {
+  const float s = fp8_scale_from_bits(*amax_bits_then_scale);
+  *reinterpret_cast<float*>(amax_bits_then_scale) = s;
+}
+
+// Split-K: y = bf16(sum_s partial[s] + bias); four outputs per thread.
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int M, int N,
+                                     const __nv_bfloat16* __restrict__ bias,
+                                     __nv_bfloat16* __restrict__ y) {
+  const int64_t total = static_cast<int64_t>(M) * N;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total; i += stride) {
+    float acc = 0.f;
+    for (int s = 0; s < splits; ++s) acc += part[static_cast<size_t>(s) * total + i];
+    if (bias != nullptr) acc += __bfloat162float(bias[i % N]);
+    y[i] = __float2bfloat16_rn(acc);
+  }
+}
+
+// ------------------------------------------------------------ device cache
+struct DeviceInfo {
+  int ok = 0;  // 1 = probed
+  int major = 0, minor = 0, sms = 0;
+  int smem_set[2][6] = {};
+};
+
+constexpr int kMaxDevices = 64;
+static DeviceInfo g_dev[kMaxDevices];
+static std::mutex g_dev_mu;
+static std::atomic<int> g_override_bm{0}, g_override_splits{0};
+
+static int current_device(DeviceInfo** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return DQ_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxDevices) return DQ_ERR_CUDA;
+  DeviceInfo& d = g_dev[dev];
+  if (!d.ok) {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (!d.ok) {
+      if (cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+          cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+          cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return DQ_ERR_CUDA;
+      d.ok = 1;
+    }
+  }
+  *out = &d;
+  if (d.major != 10) return DQ_ERR_ARCH;
+  return DQ_OK;
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+static bool make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t inner,
+                        uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                        CUtensorMapSwizzle swz) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// ----------------------------------------------------------- launch plan
+struct Plan {
+  int bm = 0, splits = 1, kb_per_split = 0;
+  int m_tiles = 0, n_tiles = 0, tiles = 0, grid = 0;
+  size_t ws = 0;
+};
+
+static int bm_index(int bm) {
+  switch (bm) {
+    case 16: return 0;
+    case 32: return 1;
+    case 64: return 2;
+    case 128: return 3;
+    case 192: return 4;
+    case 256: return 5;
+  }
+  return -1;
+}
+
+static Plan make_plan(int64_t M, int64_t N, int64_t K, int sms) {
+  Plan p;
+  const int KB = static_cast<int>((K + 63) / 64);
+  p.n_tiles = static_cast<int>((N + 127) / 128);
+  const int obm = g_override_bm.load();
+  if (obm > 0 && bm_index(obm) >= 0) {
+    p.bm = obm;
+  } else if (M <= 16) {
+    p.bm = 16;
+  } else if (M <= 32) {
+    p.bm = 32;
+  } else if (M <= 64) {
+    p.bm = 64;
+  } else if (M <= 128) {
+    p.bm = 128;
+  } else {
+    // Pick the x-tile height that minimizes (waves x tile time); 256 has a
+    // single accumulator buffer, so its epilogue does not overlap the MMAs.
+    const int cands[3] = {128, 192, 256};
+    const double penalty[3] = {1.06, 1.0, 1.08};
+    double best = 1e30;
+    for (int i = 0; i < 3; ++i) {
+      const int64_t tiles = ((M + cands[i] - 1) / cands[i]) * p.n_tiles;
+      const double waves = static_cast<double>((tiles + sms - 1) / sms);
+      const double cost = waves * cands[i] * penalty[i];
+      if (cost < best - 1e-9) { best = cost; p.bm = cands[i]; }
+    }
+  }
+  p.m_tiles = static_cast<int>((M + p.bm - 1) / p.bm);
+  const int base_tiles = p.m_tiles * p.n_tiles;
+  int s = 1;
+  const int os = g_override_splits.load();
+  if (os > 0) {
+    s = os;
+  } else if (base_tiles * 2 <= sms && KB >= 8) {
+    s = std::min(std::min(sms / base_tiles, KB / 4), 16);
+  }
+  s = std::max(1, std::min(s, KB));
+  p.kb_per_split = (KB + s - 1) / s;
+  p.splits = (KB + p.kb_per_split - 1) / p.kb_per_split;
+  p.tiles = base_tiles * p.splits;
+  p.grid = std::min(p.tiles, sms);
+  p.ws = p.splits > 1 ? static_cast<size_t>(p.splits) * M * N * sizeof(float) : 0;
+  return p;
+}
+
+template <int FMT, int BM>
+static int launch_gemm(DeviceInfo* d, const Plan& p, const CUtensorMap& mx, const CUtensorMap& mw,
+                       const GemmArgs& a, cudaStream_t st) {
+  using C = GemmCfg<FMT, BM>;
+  auto kern = dq_gemm_kernel<FMT, BM>;
+  const int bi = bm_index(BM);
+  if (!d->smem_set[FMT][bi]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
+        cudaSuccess)
+      return DQ_ERR_LAUNCH;
+    d->smem_set[FMT][bi] = 1;
+  }
+  kern<<<p.grid, C::kThreads, C::kSmemBytes, st>>>(mx, mw, a);
+  return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
+}
+
+template <int FMT>
+static int dispatch_gemm(DeviceInfo* d, const Plan& p, const CUtensorMap& mx, const CUtensorMap& mw,
+                         const GemmArgs& a, cudaStream_t st) {
+  switch (p.bm) {
+    case 16: return launch_gemm<FMT, 16>(d, p, mx, mw, a, st);
+    case 32: return launch_gemm<FMT, 32>(d, p, mx, mw, a, st);
+    case 64: return launch_gemm<FMT, 64>(d, p, mx, mw, a, st);
+    case 128: return launch_gemm<FMT, 128>(d, p, mx, mw, a, st);
+    case 192: return launch_gemm<FMT, 192>(d, p, mx, mw, a, st);
+    case 256: return launch_gemm<FMT, 256>(d, p, mx, mw, a, st);
+  }
+  return DQ_ERR_ARG;
+}
+
+static inline bool aligned(const void* p, uintptr_t a) {
+  return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
+}
+
+static int grid_for(int64_t work, int threads, int sms) {
+  int64_t g = (work + threads - 1) / threads;
+  g = std::min<int64_t>(g, static_cast<int64_t>(sms) * 16);
+  return static_cast<int>(std::max<int64_t>(g, 1));
+}
+
+static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8_t* w,
+                       const float* absmax, float scale, const void* bias, int64_t N, void* y,
+                       void* ws, size_t ws_bytes, cudaStream_t st) {
+  // NF4 blocks of 64 must lie inside a weight row; fp8 needs only 16-byte
+  // row strides for TMA (the ragged last k-block is zero-filled).
+  if (M < 0 || N <= 0 || K <= 0 || (K % (fmt == kFmtNF4 ? 64 : 16)) != 0) return DQ_ERR_SHAPE;
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return DQ_ERR_SHAPE;
+  if (M == 0) return DQ_OK;
+  if (x == nullptr || w == nullptr || y == nullptr || (fmt == kFmtNF4 && absmax == nullptr))
+    return DQ_ERR_ARG;
+  if (!aligned(x, 16) || !aligned(w, 16) || !aligned(absmax, 4) || !aligned(bias, 2) ||
+      !aligned(y, 2))
+    return DQ_ERR_ALIGN;
+  DeviceInfo* d = nullptr;
+  int rc = current_device(&d);
+  if (rc != DQ_OK) return rc;
+  const Plan p = make_plan(M, N, K, d->sms);
+  if (p.ws > 0 && (ws == nullptr || ws_bytes < p.ws || !aligned(ws, 16))) return DQ_ERR_WORKSPACE;
+
+  CUtensorMap mx, mw;
+  if (!make_map_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, M, K * 2, 64, p.bm,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+    return DQ_ERR_CUDA;
+  const uint64_t wrow = fmt == kFmtNF4 ? K / 2 : K;
+  if (!make_map_2d(&mw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, wrow, N, wrow,
+                   fmt == kFmtNF4 ? 32 : 64, 128, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return DQ_ERR_CUDA;
+
+  GemmArgs a;
+  a.absmax = absmax;
+  a.bias = static_cast<const __nv_bfloat16*>(bias);
+  a.M = static_cast<int>(M);
+  a.N = static_cast<int>(N);
+  a.K = static_cast<int>(K);
+  a.num_n_tiles = p.n_tiles;
+  a.num_tiles = p.tiles;
+  a.splits = p.splits;
+  a.kb_per_split = p.kb_per_split;
+  a.fp8_scale = scale;
+  if (p.splits > 1) {
+    a.out = ws;
+    a.vec_ok = (N % 4 == 0) && aligned(ws, 16);
+  } else {
+    a.out = y;
+    a.vec_ok = (N % 8 == 0) && aligned(y, 16);
+  }
+  rc = fmt == kFmtNF4 ? dispatch_gemm<kFmtNF4>(d, p, mx, mw, a, st)
+                      : dispatch_gemm<kFmtFP8>(d, p, mx, mw, a, st);
+  if (rc != DQ_OK) return rc;
+  if (p.splits > 1) {
+    const int64_t total = M * N;
+    splitk_reduce_kernel<<<grid_for(total, 256, d->sms), 256, 0, st>>>(
+        static_cast<const float*>(ws), p.splits, a.M, a.N, a.bias,
+        static_cast<__nv_bfloat16*>(y));
+    if (cudaGetLastError() != cudaSuccess) return DQ_ERR_LAUNCH;
+  }
+  return DQ_OK;
+}
+
+}  // namespace dq
+
+using namespace dq;
+
+extern "C" {
+
+const char* dq_version(void) { return DQ_VERSION_STRING; }
+
+int dq_abi_version(void) { return 1; }
+
+const char* dq_status_string(int s) {
+  switch (s) {
+    case DQ_OK: return "ok";
+    case DQ_ERR_SHAPE: return "bad shape (sizes must be positive, K and lengths multiples of 64)";
+    case DQ_ERR_ALIGN: return "operand not 16-byte aligned";
+    case DQ_ERR_ARCH: return "current device is not sm_100 (B200)";
+    case DQ_ERR_LAUNCH: return "kernel launch failed";
+    case DQ_ERR_TIMEOUT: return "a kernel wait timed out";
+    case DQ_ERR_WORKSPACE: return "workspace missing or too small";
+    case DQ_ERR_ARG: return "null operand or unknown enum";
+    case DQ_ERR_CUDA: return "CUDA runtime error";
+  }
+  return "unknown status";
+}
+
+int dq_quantize_nf4(const void* w, int w_dtype, int64_t n_elems, uint8_t* packed, float* absmax,
+                    dq_stream_t stream) {
+  if (n_elems < 0 || (n_elems % 64) != 0) return DQ_ERR_SHAPE;
+  if (n_elems == 0) return DQ_OK;
+  if (w == nullptr || packed == nullptr || absmax == nullptr) return DQ_ERR_ARG;
+  if (w_dtype != DQ_DTYPE_F32 && w_dtype != DQ_DTYPE_BF16) return DQ_ERR_ARG;
+  DeviceInfo* d = nullptr;
+  int rc = current_device(&d);
+  if (rc != DQ_OK) return rc;
+  const int64_t nb = n_elems / 64;
+  const int grid = grid_for(nb * 32, 256, d->sms);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (w_dtype == DQ_DTYPE_F32)
+    quantize_nf4_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(w), packed, absmax, nb);
+  else
+    quantize_nf4_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(w),
+                                                             packed, absmax, nb);
+  return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
+}
+
+int dq_quantize_fp8(const void* w, int w_dtype, int64_t n_elems, uint8_t* w8, float* scale_out,
+                    dq_stream_t stream) {
+  if (n_elems <= 0) return DQ_ERR_SHAPE;
+  if (w == nullptr || w8 == nullptr || scale_out == nullptr) return DQ_ERR_ARG;
+  if (w_dtype != DQ_DTYPE_F32 && w_dtype != DQ_DTYPE_BF16) return DQ_ERR_ARG;
+  if (!aligned(scale_out, 4)) return DQ_ERR_ALIGN;
+  DeviceInfo* d = nullptr;
+  int rc = current_device(&d);
+  if (rc != DQ_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  unsigned int* bits = reinterpret_cast<unsigned int*>(scale_out);
+  if (cudaMemsetAsync(bits, 0, sizeof(unsigned int), st) != cudaSuccess) return DQ_ERR_CUDA;
+  const int grid = grid_for(n_elems, 256, d->sms);
+  if (w_dtype == DQ_DTYPE_F32) {
+    absmax_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(w), n_elems, bits);
+    quantize_fp8_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(w), n_elems, bits, w8);
+  } else {
+    absmax_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(w), n_elems, bits);
+    quantize_fp8_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(w),
+                                                             n_elems, bits, w8);
+  }
+  finalize_fp8_scale_kernel<<<1, 1, 0, st>>>(bits);
+  return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
+}
+
+int dq_dequant_nf4(const uint8_t* packed, const float* absmax, int64_t n_elems, void* out_bf16,
+                   dq_stream_t stream) {
+  if (n_elems < 0 || (n_elems % 64) != 0) return DQ_ERR_SHAPE;
+  if (n_elems == 0) return DQ_OK;
+  if (packed == nullptr || absmax == nullptr || out_bf16 == nullptr) return DQ_ERR_ARG;
+  if (!aligned(packed, 16) || !aligned(out_bf16, 16) || !aligned(absmax, 4)) return DQ_ERR_ALIGN;
+  DeviceInfo* d = nullptr;
+  int rc = current_device(&d);
+  if (rc != DQ_OK) return rc;
+  const int64_t chunks = n_elems / 32;
+  dequant_nf4_kernel<<<grid_for(chunks, 256, d->sms), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint4*>(packed), absmax, static_cast<uint4*>(out_bf16), chunks);
+  return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
+}
+
+int dq_dequant_fp8(const uint8_t* w8, float scale, int64_t n_elems, void* out_bf16,
+                   dq_stream_t stream) {
+  if (n_elems < 0) return DQ_ERR_SHAPE;
+  if (n_elems == 0) return DQ_OK;
+  if (w8 == nullptr || out_bf16 == nullptr) return DQ_ERR_ARG;
+  if (!aligned(w8, 16) || !aligned(out_bf16, 16)) return DQ_ERR_ALIGN;
+  DeviceInfo* d = nullptr;
+  int rc = current_device(&d);
+  if (rc != DQ_OK) return rc;
+  dequant_fp8_kernel<<<grid_for(n_elems / 16 + 1, 256, d->sms), 256, 0,
+                       static_cast<cudaStream_t>(stream)>>>(w8, scale,
+                                                            static_cast<__nv_bfloat16*>(out_bf16), n_elems);
+  return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
+}
+
+size_t dq_workspace_size(int64_t M, int64_t N, int64_t K, int fmt) {
+  if (M <= 0 || N <= 0 || K <= 0 || (K % (fmt == DQ_FMT_NF4 ? 64 : 16)) != 0) return 0;
+  DeviceInfo* d = nullptr;
+  if (current_device(&d) != DQ_OK || d == nullptr) return 0;
+  return make_plan(M, N, K, d->sms).ws;
+}
+
+int dq_linear_nf4(const void* x, int64_t M, int64_t K, const uint8_t* packed, const float* absmax,
+                  const void* bias, int64_t N, void* y, void* workspace, size_t workspace_bytes,
+                  dq_stream_t stream) {
+  return linear_impl(kFmtNF4, x, M, K, packed, absmax, 0.f, bias, N, y, workspace, workspace_bytes,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int dq_linear_fp8(const void* x, int64_t M, int64_t K, const uint8_t* w8, float scale,
+                  const void* bias, int64_t N, void* y, void* workspace, size_t workspace_bytes,
+                  dq_stream_t stream) {
+  return linear_impl(kFmtFP8, x, M, K, w8, nullptr, scale, bias, N, y, workspace, workspace_bytes,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int dq_device_error(int* code, dq_stream_t stream) {
+  if (code == nullptr) return DQ_ERR_ARG;
+  unsigned int v = 0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyFromSymbolAsync(&v, g_dq_error, sizeof(v), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return DQ_ERR_CUDA;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return DQ_ERR_CUDA;
+  const unsigned int zero = 0;
+  if (v != 0 && cudaMemcpyToSymbol(g_dq_error, &zero, sizeof(zero)) != cudaSuccess) return DQ_ERR_CUDA;
+  *code = (v & (1u << kErrTimeout)) ? DQ_ERR_TIMEOUT : DQ_OK;
+  return DQ_OK;
+}
+
+int dq_set_tile_override(int bm, int splits) {
+  if (bm != 0 && bm_index(bm) < 0) return DQ_ERR_ARG;
+  if (splits < 0 || splits > 64) return DQ_ERR_ARG;
+  g_override_bm.store(bm);
+  g_override_splits.store(splits);
+  return DQ_OK;
+}
+
+}  // extern "C"

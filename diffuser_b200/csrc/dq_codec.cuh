@@ -1,0 +1,132 @@
+// dq_codec.cuh -- register-level NF4 / fp8-e4m3 codecs shared by the fused
+// GEMM, the standalone dequantizers and the quantizers.
+//
+// NF4 decode follows diffuseR's byte-LUT dequantizer (R/nf4_ltx23.R:77-115,
+// table R/jit_ltx23.R:270-281): w = RNE_bf16(bf16(level) * bf16(absmax)).
+// Here the 16 bf16 level patterns live in eight 32-bit registers (high bytes
+// and low bytes of the 16-bit patterns, four levels per register) and a
+// nibble is looked up with byte permutes instead of a memory table; the
+// product of the bf16 level and the bf16 scale is formed and rounded once by
+// the packed bf16 multiply, which equals the reference's single RNE rounding.
+#pragma once
+
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+
+namespace dq {
+
+// bf16 bit patterns of the 16 NF4 levels of R/nf4_ltx23.R:15-21
+// (double literal -> float -> bf16, round to nearest even).
+constexpr uint16_t kNf4LevelBits[16] = {0xBF80, 0xBF32, 0xBF06, 0xBECA, 0xBE92, 0xBE3D,
+                                        0xBDBA, 0x0000, 0x3DA3, 0x3E25, 0x3E7C, 0x3EAD,
+                                        0x3EE2, 0x3F10, 0x3F39, 0x3F80};
+
+// Four bytes (byte `hi` selects the high or low byte of each level pattern)
+// of levels first..first+3, packed little-endian into one register.
+__host__ __device__ constexpr uint32_t nf4_plane(int first, bool hi) {
+  uint32_t r = 0;
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t b = hi ? (kNf4LevelBits[first + i] >> 8) : (kNf4LevelBits[first + i] & 0xFFu);
+    r |= b << (8 * i);
+  }
+  return r;
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// Decode one 32-bit word of packed NF4 (bytes b0..b3 in memory order, i.e.
+// elements 0..7 with element 2j in the high nibble of byte j) into four
+// bf16x2 words in element order (element 2i in the low half of o[i]), each
+// multiplied by the bf16 scale held twice in sc2.
+__device__ __forceinline__ void nf4_decode_word(uint32_t w, uint32_t sc2, uint32_t* o) {
+  constexpr uint32_t HA = nf4_plane(0, true), HB = nf4_plane(4, true);
+  constexpr uint32_t HC = nf4_plane(8, true), HD = nf4_plane(12, true);
+  constexpr uint32_t LA = nf4_plane(0, false), LB = nf4_plane(4, false);
+  constexpr uint32_t LC = nf4_plane(8, false), LD = nf4_plane(12, false);
+  // Selector nibbles: code & 7 picks one of 8 bytes of a register pair.
+  const uint32_t s7 = w & 0x77777777u;
+  // Byte masks for codes >= 8: prmt in sign-replicate mode (selector bit 3
+  // set) copies a byte's msb over the whole byte.  The msb of byte j of w is
+  // bit 3 of its high nibble; the msb of byte j of (w << 4) is bit 3 of its
+  // low nibble.
+  const uint32_t w4 = w << 4;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const uint32_t sel = half ? (s7 >> 16) : s7;
+    // Output byte order of the lookups below: b.lo, b.hi, b'.lo, b'.hi for
+    // the two bytes b, b' of this half.
+    const uint32_t m = prmt(w, w4, half ? 0xBFAEu : 0x9D8Cu);
+    const uint32_t h = (prmt(HA, HB, sel) & ~m) | (prmt(HC, HD, sel) & m);
+    const uint32_t l = (prmt(LA, LB, sel) & ~m) | (prmt(LC, LD, sel) & m);
+    // Interleave low/high bytes into bf16 pairs: (hi nibble, lo nibble) of b,
+    // then of b'.
+    o[2 * half + 0] = bf16x2_mul(prmt(l, h, 0x4051u), sc2);
+    o[2 * half + 1] = bf16x2_mul(prmt(l, h, 0x6273u), sc2);
+  }
+}
+
+__device__ __forceinline__ uint32_t bf16_bits(float v) {
+  return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v)));
+}
+
+// absmax$to(bf16), replicated into both halves.
+__device__ __forceinline__ uint32_t nf4_scale2(float absmax) {
+  const uint32_t b = bf16_bits(absmax);
+  return b | (b << 16);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// Decode one 32-bit word of e4m3 (elements 0..3 in memory order) into two
+// bf16x2 words: RNE_bf16(e4m3 * s) where s is the bf16-rounded scale held as
+// f32.  e4m3 -> f16 -> f32 is exact and the f32 product of a 4-bit and an
+// 8-bit significand is exact, so the final conversion is the only rounding,
+// as in R/fp8_ltx23.R:79-80.
+__device__ __forceinline__ void fp8_decode_word(uint32_t w, float s, uint32_t* o) {
+  const __half2_raw h01 =
+      __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w & 0xFFFFu), __NV_E4M3);
+  const __half2_raw h23 =
+      __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w >> 16), __NV_E4M3);
+  const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
+  const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
+  o[0] = pack_bf16x2(f01.x * s, f01.y * s);
+  o[1] = pack_bf16x2(f23.x * s, f23.y * s);
+}
+
+// bucketize(v, midpoints, right = FALSE): number of midpoints strictly below v.
+// The midpoints are (level[i] + level[i+1]) / 2 computed in float32 exactly as
+// R/nf4_ltx23.R:46 does.
+__device__ __forceinline__ uint32_t nf4_code(float v) {
+  constexpr float kMid[15] = {
+      -0x1.b239b0p-1f, -0x1.38a4e0p-1f, -0x1.d70900p-2f, -0x1.5bd4ecp-2f, -0x1.e079d8p-3f,
+      -0x1.1a7178p-3f, -0x1.74f0e2p-5f, 0x1.45f5fep-5f,  0x1.ec90c4p-4f,  0x1.a0cfc0p-3f,
+      0x1.2b05a8p-2f,  0x1.8ea7f2p-2f,  0x1.00da08p-1f,  0x1.491b5ep-1f,  0x1.b913b4p-1f};
+  uint32_t c = 0;
+#pragma unroll
+  for (int i = 0; i < 15; ++i) c += (kMid[i] < v) ? 1u : 0u;
+  return c;
+}
+
+// float32 -> e4m3fn, round to nearest even; magnitudes above 464 become NaN
+// as in c10::Float8_e4m3fn (a quantized weight never reaches them).
+__device__ __forceinline__ uint8_t f32_to_e4m3(float v) {
+  if (fabsf(v) > 464.0f) return static_cast<uint8_t>(0x7Fu | (v < 0.0f ? 0x80u : 0u));
+  return static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
+}
+
+}  // namespace dq

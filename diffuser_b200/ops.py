@@ -1,0 +1,223 @@
+"""Torch-facing wrappers over the C ABI: every op runs the sm_100a kernels.
+
+These mirror the functional half of diffuseR's quantized-linear API
+(R/nf4_ltx23.R, R/fp8_ltx23.R).  Tensors are passed to the library as raw
+device pointers with torch's current CUDA stream.  There is no CPU path: a
+CPU tensor, a non-bf16 activation or a missing library raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from . import _lib
+
+NF4_BLOCK = 64  # R/nf4_ltx23.R:23
+
+
+def _require_cuda(t: torch.Tensor, name: str) -> None:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor: the engine has no CPU path")
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.float32:
+        return _lib.DQ_DTYPE_F32
+    if t.dtype == torch.bfloat16:
+        return _lib.DQ_DTYPE_BF16
+    raise TypeError(f"unsupported weight dtype {t.dtype}; expected float32 or bfloat16")
+
+
+# ------------------------------------------------------------- workspaces
+_WS_LOCK = threading.Lock()
+_WS: dict = {}
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
+    """Per-device scratch for split-K partial sums, grown on demand and reused
+    (the analogue of the reference's per-shape dequant buffers,
+    R/nf4_ltx23.R:160-175, except that it holds f32 partials, not weights)."""
+    if nbytes == 0:
+        return None
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    with _WS_LOCK:
+        buf = _WS.get(idx)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(nbytes, dtype=torch.uint8, device=torch.device("cuda", idx))
+            _WS[idx] = buf
+        return buf
+
+
+def release_workspaces() -> None:
+    """Drop the cached scratch (ltx23_release_dequant_buffers, R/nf4_ltx23.R:185-194)."""
+    with _WS_LOCK:
+        _WS.clear()
+
+
+def workspace_size(M: int, N: int, K: int, fmt: int = _lib.DQ_FMT_NF4) -> int:
+    return int(_lib.lib().dq_workspace_size(M, N, K, fmt))
+
+
+# ----------------------------------------------------------------- quantize
+def ltx23_nf4_quantize(x: torch.Tensor):
+    """NF4-quantize a CUDA tensor (R/nf4_ltx23.R:35-61).
+
+    Returns ``(packed uint8 [n/2], absmax float32 [n/64])``; ``n`` must be a
+    multiple of 64 (the reference's error otherwise).
+    """
+    _require_cuda(x, "x")
+    n = x.numel()
+    if n % NF4_BLOCK != 0:
+        raise ValueError(f"Tensor length must be a multiple of {NF4_BLOCK}")
+    src = x.detach()
+    if src.dtype not in (torch.float32, torch.bfloat16):
+        src = src.to(torch.float32)
+    src = src.contiguous()
+    packed = torch.empty(n // 2, dtype=torch.uint8, device=x.device)
+    absmax = torch.empty(n // NF4_BLOCK, dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        _lib.check("dq_quantize_nf4", _lib.lib().dq_quantize_nf4(
+            _ptr(src), _dtype_code(src), n, _ptr(packed), _ptr(absmax), _stream(x.device)))
+    return packed, absmax
+
+
+def fp8_quantize(x: torch.Tensor):
+    """Per-tensor e4m3 quantization (R/quantize_flux.R:406-409).
+
+    Returns ``(w8 float8_e4m3fn, scale float32 0-d tensor)``, both on x's device.
+    """
+    _require_cuda(x, "x")
+    src = x.detach()
+    if src.dtype not in (torch.float32, torch.bfloat16):
+        src = src.to(torch.float32)
+    src = src.contiguous()
+    w8 = torch.empty(src.shape, dtype=torch.uint8, device=x.device)
+    scale = torch.empty((), dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        _lib.check("dq_quantize_fp8", _lib.lib().dq_quantize_fp8(
+            _ptr(src), _dtype_code(src), src.numel(), _ptr(w8), _ptr(scale), _stream(x.device)))
+    return w8.view(torch.float8_e4m3fn), scale
+
+
+# --------------------------------------------------------------- dequantize
+def ltx23_nf4_dequantize(packed: torch.Tensor, absmax: torch.Tensor, shape,
+                         dtype=torch.bfloat16, out: torch.Tensor | None = None) -> torch.Tensor:
+    """NF4 -> bf16 (R/nf4_ltx23.R:77-115), bit-exact with the byte-LUT path."""
+    _require_cuda(packed, "packed")
+    if dtype != torch.bfloat16:
+        raise TypeError("the engine dequantizes to bfloat16 only")
+    n = 1
+    for s in shape:
+        n *= int(s)
+    if packed.numel() * 2 != n or absmax.numel() * NF4_BLOCK != n:
+        raise ValueError("packed / absmax sizes do not match shape")
+    if out is None:
+        out = torch.empty(tuple(shape), dtype=torch.bfloat16, device=packed.device)
+    am = absmax if absmax.dtype == torch.float32 else absmax.float()
+    with torch.cuda.device(packed.device):
+        _lib.check("dq_dequant_nf4", _lib.lib().dq_dequant_nf4(
+            _ptr(packed.contiguous()), _ptr(am.contiguous()), n, _ptr(out), _stream(packed.device)))
+    return out
+
+
+def fp8_dequantize(w8: torch.Tensor, scale, dtype=torch.bfloat16,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """e4m3 -> bf16 times bf16(scale) (R/fp8_ltx23.R:79-80), bit-exact."""
+    _require_cuda(w8, "w8")
+    if dtype != torch.bfloat16:
+        raise TypeError("the engine dequantizes to bfloat16 only")
+    s = float(scale)
+    if out is None:
+        out = torch.empty(w8.shape, dtype=torch.bfloat16, device=w8.device)
+    raw = w8.contiguous().view(torch.uint8)
+    with torch.cuda.device(w8.device):
+        _lib.check("dq_dequant_fp8", _lib.lib().dq_dequant_fp8(
+            _ptr(raw), ctypes.c_float(s), raw.numel(), _ptr(out), _stream(w8.device)))
+    return out
+
+
+# ------------------------------------------------------------------- linear
+def _prep_x(x: torch.Tensor, k: int) -> torch.Tensor:
+    _require_cuda(x, "x")
+    if x.dtype != torch.bfloat16:
+        raise TypeError(f"activations must be bfloat16 on the GPU path, got {x.dtype}")
+    if x.shape[-1] != k:
+        raise ValueError(f"last dim of x is {x.shape[-1]}, expected in_features={k}")
+    x2 = x.reshape(-1, k)
+    if not x2.is_contiguous() or x2.data_ptr() % 16 != 0:
+        x2 = x2.contiguous()
+    return x2
+
+
+def _prep_bias(bias, n: int, device):
+    if bias is None:
+        return None
+    b = bias.detach()
+    if b.dtype != torch.bfloat16:
+        b = b.to(torch.bfloat16)
+    if b.device != device:
+        b = b.to(device)
+    if b.numel() != n:
+        raise ValueError("bias size does not match out_features")
+    return b.contiguous()
+
+
+def nf4_linear(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor,
+               out_features: int, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x . dequant_nf4(W)^T + bias in one fused kernel (R/nf4_ltx23.R:235-246)."""
+    n = int(out_features)
+    k = packed.numel() * 2 // n
+    x2 = _prep_x(x, k)
+    m = x2.shape[0]
+    y = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    b = _prep_bias(bias, n, x.device)
+    am = absmax if absmax.dtype == torch.float32 else absmax.float()
+    with torch.cuda.device(x.device):
+        ws_bytes = workspace_size(m, n, k, _lib.DQ_FMT_NF4)
+        ws = workspace(x.device, ws_bytes)
+        _lib.check("dq_linear_nf4", _lib.lib().dq_linear_nf4(
+            _ptr(x2), m, k, _ptr(packed), _ptr(am), _ptr(b), n, _ptr(y),
+            _ptr(ws), ws_bytes, _stream(x.device)))
+    return y.reshape(*x.shape[:-1], n)
+
+
+def fp8_linear(x: torch.Tensor, w8: torch.Tensor, scale: float,
+               bias: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x . (e4m3(W) * bf16(scale))^T + bias fused (R/fp8_ltx23.R:70-83)."""
+    n, k = int(w8.shape[0]), int(w8.shape[1])
+    x2 = _prep_x(x, k)
+    m = x2.shape[0]
+    y = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    b = _prep_bias(bias, n, x.device)
+    raw = w8.view(torch.uint8)
+    with torch.cuda.device(x.device):
+        ws_bytes = workspace_size(m, n, k, _lib.DQ_FMT_FP8)
+        ws = workspace(x.device, ws_bytes)
+        _lib.check("dq_linear_fp8", _lib.lib().dq_linear_fp8(
+            _ptr(x2), m, k, _ptr(raw), ctypes.c_float(float(scale)), _ptr(b), n, _ptr(y),
+            _ptr(ws), ws_bytes, _stream(x.device)))
+    return y.reshape(*x.shape[:-1], n)
+
+
+def device_error(device=None) -> int:
+    """Read and clear the device's kernel error word (DQ_OK or DQ_ERR_TIMEOUT)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    code = ctypes.c_int(0)
+    with torch.cuda.device(dev):
+        _lib.check("dq_device_error", _lib.lib().dq_device_error(ctypes.byref(code), _stream(dev)))
+    return code.value
+
+
+def set_tile_override(bm: int = 0, splits: int = 0) -> None:
+    """Force the x-tile height / split-K count (0 = automatic); for sweeps."""
+    _lib.check("dq_set_tile_override", _lib.lib().dq_set_tile_override(int(bm), int(splits)))

@@ -1,0 +1,116 @@
+/*
+ * dq_linear.h -- C ABI of the B200 (sm_100a) quantized weight-only linear
+ * engine for diffuseR's NF4 and fp8-e4m3 linears.
+ *
+ * Every entry point takes plain device pointers and sizes plus a CUDA stream,
+ * allocates nothing (scratch comes from the caller's workspace), never aborts
+ * and returns a dq_status.  Work is enqueued on `stream`; kernels that hit a
+ * bounded wait record DQ_ERR_TIMEOUT in a per-device error word readable with
+ * dq_device_error().
+ *
+ * Layouts are the reference's (diffuseR 0.2.2):
+ *   x       bf16 [M, K] row-major (any leading dims flattened into M)
+ *   packed  uint8 [N*K/2]   NF4 codes, element 2j in the HIGH nibble of byte j
+ *   absmax  f32  [N*K/64]   one scale per 64 consecutive weight elements
+ *   w8      e4m3fn [N, K]   fp8 weight, per-tensor fp32 scale
+ *   bias    bf16 [N] or NULL
+ *   y       bf16 [M, N]
+ * Requirements: K % 64 == 0 for NF4 (blocks lie inside a weight row),
+ * K % 16 == 0 for fp8; x, packed/w8 and y 16-byte aligned.
+ */
+#ifndef DQ_LINEAR_H
+#define DQ_LINEAR_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Opaque stream handle: a cudaStream_t (0 = legacy default stream). */
+typedef void* dq_stream_t;
+
+typedef enum dq_status {
+  DQ_OK = 0,
+  DQ_ERR_SHAPE = 1,     /* non-positive size, bad K (see above), length % 64 != 0 */
+  DQ_ERR_ALIGN = 2,     /* an operand is not 16-byte aligned */
+  DQ_ERR_ARCH = 3,      /* current device is not sm_100 (B200 / GB200) */
+  DQ_ERR_LAUNCH = 4,    /* a kernel launch failed */
+  DQ_ERR_TIMEOUT = 5,   /* a kernel's bounded wait expired (dq_device_error) */
+  DQ_ERR_WORKSPACE = 6, /* workspace NULL or smaller than dq_workspace_size() */
+  DQ_ERR_ARG = 7,       /* NULL operand pointer or unknown enum value */
+  DQ_ERR_CUDA = 8       /* another CUDA runtime error */
+} dq_status;
+
+typedef enum dq_format { DQ_FMT_NF4 = 0, DQ_FMT_FP8 = 1 } dq_format;
+
+typedef enum dq_dtype { DQ_DTYPE_F32 = 0, DQ_DTYPE_BF16 = 1 } dq_dtype;
+
+/* Library version string and the ABI revision of this header. */
+const char* dq_version(void);
+int dq_abi_version(void);
+const char* dq_status_string(int status);
+
+/* ---------------------------------------------------------------- quantize
+ * NF4 quantizer.  Replaces ltx23_nf4_quantize (R/nf4_ltx23.R:35-61):
+ * per 64-element block absmax (f32, clamped >= 1e-12), normalized = w/absmax,
+ * code = bucketize(normalized, f32 level midpoints, right = FALSE), two codes
+ * per byte (first in the high nibble).  n_elems % 64 == 0.
+ * w is f32 or bf16 (w_dtype); outputs packed [n/2] and absmax [n/64]. */
+int dq_quantize_nf4(const void* w, int w_dtype, int64_t n_elems,
+                    uint8_t* packed, float* absmax, dq_stream_t stream);
+
+/* Per-tensor fp8-e4m3 quantizer.  Replaces the cast branch of flux_quantize
+ * (R/quantize_flux.R:406-409) and ltx23_quantize_fp8 (R/fp8_ltx23.R:178-181):
+ * scale = max(max|w|, 1e-12) / 448 (f32), w8 = e4m3fn(w / scale).
+ * Writes the scale to the device float *scale_out. */
+int dq_quantize_fp8(const void* w, int w_dtype, int64_t n_elems,
+                    uint8_t* w8, float* scale_out, dq_stream_t stream);
+
+/* -------------------------------------------------------------- dequantize
+ * NF4 -> bf16.  Replaces ltx23_nf4_dequantize(dtype = bf16)
+ * (R/nf4_ltx23.R:77-115 with the byte LUT of R/jit_ltx23.R:270-281):
+ * out = RNE_bf16(bf16(level) * bf16(absmax)), bit-exact. */
+int dq_dequant_nf4(const uint8_t* packed, const float* absmax, int64_t n_elems,
+                   void* out_bf16, dq_stream_t stream);
+
+/* e4m3 -> bf16.  Replaces the upcast + rescale of ltx23_fp8_linear$forward
+ * (R/fp8_ltx23.R:79-80): out = RNE_bf16(e4m3 * bf16(scale)), bit-exact. */
+int dq_dequant_fp8(const uint8_t* w8, float scale, int64_t n_elems,
+                   void* out_bf16, dq_stream_t stream);
+
+/* ------------------------------------------------------------------ linear
+ * Bytes of caller-provided scratch the linear needs for this shape (split-K
+ * partial sums; 0 when the shape runs unsplit). */
+size_t dq_workspace_size(int64_t M, int64_t N, int64_t K, int fmt);
+
+/* y = x . dequant(W)^T + bias, dequantization fused into a tcgen05 GEMM.
+ * Replaces ltx23_nf4_linear$forward (R/nf4_ltx23.R:235-246) and the
+ * TorchScript nf4_lin (R/jit_ltx23.R:40-50). */
+int dq_linear_nf4(const void* x, int64_t M, int64_t K,
+                  const uint8_t* packed, const float* absmax,
+                  const void* bias, int64_t N, void* y,
+                  void* workspace, size_t workspace_bytes, dq_stream_t stream);
+
+/* Same for fp8-e4m3 with a per-tensor scale passed by value.
+ * Replaces ltx23_fp8_linear$forward (R/fp8_ltx23.R:70-83). */
+int dq_linear_fp8(const void* x, int64_t M, int64_t K,
+                  const uint8_t* w8, float scale,
+                  const void* bias, int64_t N, void* y,
+                  void* workspace, size_t workspace_bytes, dq_stream_t stream);
+
+/* ---------------------------------------------------------------- errors
+ * Reads and clears the current device's kernel error word (synchronizes
+ * `stream`).  *code receives DQ_OK or DQ_ERR_TIMEOUT. */
+int dq_device_error(int* code, dq_stream_t stream);
+
+/* Kernel-configuration override for benchmarking sweeps: x-tile rows
+ * (16..256, multiple of 16; 0 = automatic) and split-K count (0 = auto). */
+int dq_set_tile_override(int bm, int splits);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DQ_LINEAR_H */

@@ -1,0 +1,88 @@
+"""CPU tests of the C-ABI library: it builds for sm_100a, loads without a GPU,
+exports every symbol the header declares, and rejects bad arguments on the
+host before touching a device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from diffuser_b200 import _lib
+from diffuser_b200 import build as B
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                      "include", "dq_linear.h")
+
+
+def _header_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(dq_[a-z0-9_]+)\s*\(", src)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    B.build()
+    return _lib.lib()
+
+
+def test_header_declares_expected_entry_points():
+    names = _header_functions()
+    for must in ("dq_linear_nf4", "dq_linear_fp8", "dq_dequant_nf4", "dq_dequant_fp8",
+                 "dq_quantize_nf4", "dq_quantize_fp8", "dq_workspace_size", "dq_version"):
+        assert must in names
+
+
+def test_library_exports_every_header_symbol(lib):
+    for name in _header_functions():
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"binding missing for {name}"
+
+
+def test_version_and_status_strings(lib):
+    assert "sm_100a" in _lib.version()
+    assert lib.dq_abi_version() == 1
+    assert _lib.status_string(0) == "ok"
+    assert "shape" in _lib.status_string(1)
+
+
+def test_shape_errors_rejected_on_host(lib):
+    p = ctypes.c_void_p(16)
+    # K not a multiple of 64
+    assert lib.dq_linear_nf4(p, 4, 100, p, p, None, 8, p, None, 0, None) == 1
+    assert lib.dq_linear_fp8(p, 4, 100, p, ctypes.c_float(1.0), None, 8, p, None, 0, None) == 1
+    # non-positive N / K
+    assert lib.dq_linear_nf4(p, 4, 64, p, p, None, 0, p, None, 0, None) == 1
+    assert lib.dq_linear_nf4(p, 4, -64, p, p, None, 8, p, None, 0, None) == 1
+    # lengths not a multiple of 64
+    assert lib.dq_dequant_nf4(p, p, 100, p, None) == 1
+    assert lib.dq_quantize_nf4(p, 0, 100, p, p, None) == 1
+
+
+def test_null_and_alignment_errors_rejected_on_host(lib):
+    p = ctypes.c_void_p(4096)
+    odd = ctypes.c_void_p(4096 + 8)
+    assert lib.dq_linear_nf4(None, 4, 64, p, p, None, 8, p, None, 0, None) == 7
+    assert lib.dq_linear_nf4(p, 4, 64, p, None, None, 8, p, None, 0, None) == 7
+    assert lib.dq_linear_nf4(odd, 4, 64, p, p, None, 8, p, None, 0, None) == 2
+    assert lib.dq_linear_fp8(p, 4, 64, odd, ctypes.c_float(1.0), None, 8, p, None, 0, None) == 2
+    assert lib.dq_dequant_nf4(odd, p, 64, p, None) == 2
+    assert lib.dq_quantize_nf4(p, 5, 64, p, p, None) == 7
+    assert lib.dq_set_tile_override(48, 0) == 7
+    assert lib.dq_set_tile_override(0, 0) == 0
+
+
+def test_empty_batch_is_a_noop(lib):
+    p = ctypes.c_void_p(4096)
+    assert lib.dq_linear_nf4(p, 0, 64, p, p, None, 8, p, None, 0, None) == 0
+    assert lib.dq_dequant_nf4(p, p, 0, p, None) == 0
+
+
+def test_product_path_refuses_cpu_tensors():
+    import torch
+    from diffuser_b200 import ops
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.nf4_linear(torch.zeros(2, 64, dtype=torch.bfloat16),
+                       torch.zeros(64 * 8 // 2, dtype=torch.uint8), torch.ones(8), 8)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.ltx23_nf4_quantize(torch.zeros(64))

@@ -1,0 +1,169 @@
+"""GPU parity of the fused NF4 / fp8 linear against the oracle.
+
+Tolerance (the contract stated for the GEMM): max|y - y_ref| / max|y_ref| <= 1e-2,
+where y_ref is the oracle's dequantize-then-matmul in float64 on the
+bit-identical bf16 weights, rounded once to bf16.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import numpy_ref as R
+from tests.gpu_util import from_bits, seeded_bf16, seeded_f32, to_bits
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from diffuser_b200 import ops as _ops
+    yield _ops
+    _ops.set_tile_override(0, 0)
+
+
+def _case(m, n, k, seed, fmt, with_bias):
+    x = seeded_bf16((m, k), seed)
+    w = seeded_f32((n, k), seed + 1000, 0.02)
+    bias = seeded_bf16((n,), seed + 2000, 0.5) if with_bias else None
+    xb = to_bits(x)
+    bb = to_bits(bias) if with_bias else None
+    if fmt == "nf4":
+        p, a = R.nf4_quantize(w.numpy())
+        ref = R.nf4_linear_bf16(xb, p, a, n, k, bb)
+        return x, (torch.from_numpy(p).cuda(), torch.from_numpy(a).cuda()), bias, ref
+    w8, s = R.fp8_quantize(w.numpy())
+    ref = R.fp8_linear_bf16(xb, w8, s, n, k, bb)
+    return x, (torch.from_numpy(w8).cuda().view(torch.float8_e4m3fn), float(s)), bias, ref
+
+
+def _run(ops, fmt, x, w, bias, n):
+    xc = x.cuda()
+    bc = bias.cuda() if bias is not None else None
+    if fmt == "nf4":
+        return ops.nf4_linear(xc, w[0], w[1], n, bc)
+    return ops.fp8_linear(xc, w[0], w[1], bc)
+
+
+SHAPES = [(1, 64, 64), (5, 64, 128), (7, 200, 192), (16, 128, 256), (65, 130, 256),
+          (128, 128, 128), (200, 384, 640), (257, 1000, 1024), (600, 512, 3072)]
+
+
+@pytest.mark.parametrize("fmt", ["nf4", "fp8"])
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_linear_matches_oracle(ops, fmt, m, n, k):
+    x, w, bias, ref = _case(m, n, k, m * 7 + n, fmt, with_bias=(m % 2 == 1))
+    y = _run(ops, fmt, x, w, bias, n)
+    torch.cuda.synchronize()
+    assert y.shape == (m, n) and y.dtype == torch.bfloat16
+    err = R.rel_err(to_bits(y), ref)
+    assert err <= TOL, err
+
+
+@pytest.mark.parametrize("m,n,k", [(3, 48, 96), (70, 200, 80), (130, 136, 1040)])
+def test_fp8_ragged_k(ops, m, n, k):
+    # fp8 has no block structure: K need only keep 16-byte row strides
+    x, w, bias, ref = _case(m, n, k, 31 + k, "fp8", with_bias=True)
+    y = _run(ops, "fp8", x, w, bias, n)
+    assert R.rel_err(to_bits(y), ref) <= TOL
+
+
+@pytest.mark.parametrize("fmt", ["nf4", "fp8"])
+@pytest.mark.parametrize("bm", [16, 32, 64, 128, 192, 256])
+def test_every_tile_height(ops, fmt, bm):
+    m, n, k = 300, 640, 512
+    x, w, bias, ref = _case(m, n, k, bm, fmt, with_bias=True)
+    ops.set_tile_override(bm, 0)
+    try:
+        y = _run(ops, fmt, x, w, bias, n)
+        torch.cuda.synchronize()
+    finally:
+        ops.set_tile_override(0, 0)
+    assert R.rel_err(to_bits(y), ref) <= TOL
+
+
+@pytest.mark.parametrize("fmt", ["nf4", "fp8"])
+@pytest.mark.parametrize("m,n,k,splits", [(1, 1024, 4096, 0), (16, 3072, 3072, 0),
+                                          (64, 2304, 3072, 5), (3, 200, 1088, 3)])
+def test_split_k(ops, fmt, m, n, k, splits):
+    x, w, bias, ref = _case(m, n, k, 17 + m, fmt, with_bias=True)
+    ops.set_tile_override(0, splits)
+    try:
+        y = _run(ops, fmt, x, w, bias, n)
+        torch.cuda.synchronize()
+    finally:
+        ops.set_tile_override(0, 0)
+    assert R.rel_err(to_bits(y), ref) <= TOL
+
+
+def test_leading_dims_and_noncontiguous_input(ops):
+    m, n, k = 24, 192, 256
+    x, w, bias, ref = _case(m, n, k, 5, "nf4", with_bias=True)
+    x3 = x.reshape(2, 12, k).cuda()
+    y = ops.nf4_linear(x3, w[0], w[1], n, bias.cuda())
+    assert y.shape == (2, 12, n)
+    assert R.rel_err(to_bits(y.reshape(m, n)), ref) <= TOL
+    xt = x.cuda().t().contiguous().t()  # same values, column-major storage
+    y2 = ops.nf4_linear(xt, w[0], w[1], n, bias.cuda())
+    assert torch.equal(y2, y.reshape(m, n))
+
+
+def test_deterministic_repeat(ops):
+    m, n, k = 333, 1280, 1024
+    x, w, bias, _ = _case(m, n, k, 9, "nf4", with_bias=True)
+    a = _run(ops, "nf4", x, w, bias, n)
+    b = _run(ops, "nf4", x, w, bias, n)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+
+
+def _full_size_check(ops, fmt):
+    # The NF4 / fp8 linear at the benchmarked shape: x [4608, 3072], W [12288, 3072].
+    m, n, k = 4608, 12288, 3072
+    g = torch.Generator(device="cuda").manual_seed(1)
+    x = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
+    g0 = torch.Generator(device="cuda").manual_seed(0)
+    w = torch.randn(n, k, generator=g0, device="cuda") * 0.02
+    if fmt == "nf4":
+        p, a = ops.ltx23_nf4_quantize(w)
+        y = ops.nf4_linear(x, p, a, n)
+        wd = ops.ltx23_nf4_dequantize(p, a, (n, k))
+    else:
+        w8, s = ops.fp8_quantize(w)
+        y = ops.fp8_linear(x, w8, s.item())
+        wd = ops.fp8_dequantize(w8, s.item())
+    # cuBLAS on the bit-exact dequantized weight = the reference's GPU algorithm
+    ref = (x.float() @ wd.float().t()).to(torch.bfloat16)
+    err = ((y.float() - ref.float()).abs().max() / ref.float().abs().max()).item()
+    assert err <= TOL, err
+    # exact oracle on a sample of rows
+    rows = torch.arange(0, m, 97, device="cuda")
+    yb = to_bits(y[rows])
+    ref_rows = R.linear_bf16(to_bits(x[rows]), to_bits(wd), None)
+    assert R.rel_err(yb, ref_rows) <= TOL
+    return y
+
+
+def test_full_size_nf4(ops):
+    _full_size_check(ops, "nf4")
+
+
+def test_full_size_fp8(ops):
+    _full_size_check(ops, "fp8")
+
+
+def test_golden_linear(ops):
+    import os
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "quant_linear_golden.npz"))
+    y = ops.nf4_linear(from_bits(g["nf4_x"]), torch.from_numpy(g["nf4_packed"]).cuda(),
+                       torch.from_numpy(g["nf4_absmax"]).cuda(), 64, from_bits(g["nf4_bias"]))
+    assert R.rel_err(to_bits(y), g["nf4_y"]) <= TOL
+    y2 = ops.fp8_linear(from_bits(g["fp8_x"]),
+                        torch.from_numpy(g["fp8_w8"]).cuda().view(torch.float8_e4m3fn),
+                        float(g["fp8_scale"]), from_bits(g["fp8_bias"]))
+    assert R.rel_err(to_bits(y2), g["fp8_y"]) <= TOL
+
+
+def test_no_kernel_error_recorded(ops):
+    assert ops.device_error() == 0
