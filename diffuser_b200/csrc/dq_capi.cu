@@ -25,12 +25,12 @@ __global__ void dequant_nf4_kernel(const uint4* __restrict__ packed, const float
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n_chunks;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const uint4 p = __ldg(packed + i);
-    const uint32_t sc2 = nf4_scale2(__ldg(absmax + (i >> 1)));
+    const Nf4Planes planes = nf4_scaled_planes(nf4_scale2(__ldg(absmax + (i >> 1))));
     uint32_t o[16];
-    nf4_decode_word(p.x, sc2, o + 0);
-    nf4_decode_word(p.y, sc2, o + 4);
-    nf4_decode_word(p.z, sc2, o + 8);
-    nf4_decode_word(p.w, sc2, o + 12);
+    nf4_decode_word(p.x, planes, o + 0);
+    nf4_decode_word(p.y, planes, o + 4);
+    nf4_decode_word(p.z, planes, o + 8);
+    nf4_decode_word(p.w, planes, o + 12);
     uint4* dst = out + 4 * i;
 #pragma unroll
     for (int j = 0; j < 4; ++j) dst[j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);

@@ -3,11 +3,11 @@
 //
 // NF4 decode follows diffuseR's byte-LUT dequantizer (R/nf4_ltx23.R:77-115,
 // table R/jit_ltx23.R:270-281): w = RNE_bf16(bf16(level) * bf16(absmax)).
-// Here the 16 bf16 level patterns live in eight 32-bit registers (high bytes
-// and low bytes of the 16-bit patterns, four levels per register) and a
-// nibble is looked up with byte permutes instead of a memory table; the
-// product of the bf16 level and the bf16 scale is formed and rounded once by
-// the packed bf16 multiply, which equals the reference's single RNE rounding.
+// Here, per 64-element block, the 16 levels are first multiplied by the bf16
+// block scale with the packed bf16 multiply (one RNE rounding of an exact
+// product, as in the reference), then split into byte planes held in eight
+// 32-bit registers, and every 4-bit code is looked up with byte permutes
+// instead of a memory table.
 #pragma once
 
 #include <cstdint>
@@ -46,15 +46,43 @@ __device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
   return d;
 }
 
+// The 16 levels multiplied by one bf16 block scale and rounded once
+// (RNE_bf16(bf16(level) * bf16(absmax)), the reference's dequantized value),
+// split into byte planes for the permute lookups: ha..hd hold the high bytes of
+// levels 0-3, 4-7, 8-11, 12-15 and la..ld the low bytes.
+struct Nf4Planes {
+  uint32_t ha, hb, hc, hd, la, lb, lc, ld;
+};
+
+__host__ __device__ constexpr uint32_t nf4_level_pair(int i) {
+  return static_cast<uint32_t>(kNf4LevelBits[2 * i]) |
+         (static_cast<uint32_t>(kNf4LevelBits[2 * i + 1]) << 16);
+}
+
+__device__ __forceinline__ Nf4Planes nf4_scaled_planes(uint32_t sc2) {
+  constexpr uint32_t kPairs[8] = {nf4_level_pair(0), nf4_level_pair(1), nf4_level_pair(2),
+                                  nf4_level_pair(3), nf4_level_pair(4), nf4_level_pair(5),
+                                  nf4_level_pair(6), nf4_level_pair(7)};
+  uint32_t q[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) q[i] = bf16x2_mul(kPairs[i], sc2);
+  Nf4Planes p;
+  p.ha = prmt(q[0], q[1], 0x7531u);
+  p.la = prmt(q[0], q[1], 0x6420u);
+  p.hb = prmt(q[2], q[3], 0x7531u);
+  p.lb = prmt(q[2], q[3], 0x6420u);
+  p.hc = prmt(q[4], q[5], 0x7531u);
+  p.lc = prmt(q[4], q[5], 0x6420u);
+  p.hd = prmt(q[6], q[7], 0x7531u);
+  p.ld = prmt(q[6], q[7], 0x6420u);
+  return p;
+}
+
 // Decode one 32-bit word of packed NF4 (bytes b0..b3 in memory order, i.e.
 // elements 0..7 with element 2j in the high nibble of byte j) into four
-// bf16x2 words in element order (element 2i in the low half of o[i]), each
-// multiplied by the bf16 scale held twice in sc2.
-__device__ __forceinline__ void nf4_decode_word(uint32_t w, uint32_t sc2, uint32_t* o) {
-  constexpr uint32_t HA = nf4_plane(0, true), HB = nf4_plane(4, true);
-  constexpr uint32_t HC = nf4_plane(8, true), HD = nf4_plane(12, true);
-  constexpr uint32_t LA = nf4_plane(0, false), LB = nf4_plane(4, false);
-  constexpr uint32_t LC = nf4_plane(8, false), LD = nf4_plane(12, false);
+// bf16x2 words in element order (element 2i in the low half of o[i]), looking
+// each code up in the scaled planes.
+__device__ __forceinline__ void nf4_decode_word(uint32_t w, const Nf4Planes& P, uint32_t* o) {
   // Selector nibbles: code & 7 picks one of 8 bytes of a register pair.
   const uint32_t s7 = w & 0x77777777u;
   // Byte masks for codes >= 8: prmt in sign-replicate mode (selector bit 3
@@ -68,12 +96,47 @@ __device__ __forceinline__ void nf4_decode_word(uint32_t w, uint32_t sc2, uint32
     // Output byte order of the lookups below: b.lo, b.hi, b'.lo, b'.hi for
     // the two bytes b, b' of this half.
     const uint32_t m = prmt(w, w4, half ? 0xBFAEu : 0x9D8Cu);
-    const uint32_t h = (prmt(HA, HB, sel) & ~m) | (prmt(HC, HD, sel) & m);
-    const uint32_t l = (prmt(LA, LB, sel) & ~m) | (prmt(LC, LD, sel) & m);
+    const uint32_t h = (prmt(P.ha, P.hb, sel) & ~m) | (prmt(P.hc, P.hd, sel) & m);
+    const uint32_t l = (prmt(P.la, P.lb, sel) & ~m) | (prmt(P.lc, P.ld, sel) & m);
     // Interleave low/high bytes into bf16 pairs: (hi nibble, lo nibble) of b,
     // then of b'.
-    o[2 * half + 0] = bf16x2_mul(prmt(l, h, 0x4051u), sc2);
-    o[2 * half + 1] = bf16x2_mul(prmt(l, h, 0x6273u), sc2);
+    o[2 * half + 0] = prmt(l, h, 0x4051u);
+    o[2 * half + 1] = prmt(l, h, 0x6273u);
+  }
+}
+
+// Shared-memory byte LUT for NF4: entry b is the bf16 pair (level[b >> 4] in
+// the low half, level[b & 15] in the high half), i.e. the two elements of a
+// packed byte in order -- the reference's [256, 2] byte table
+// (R/jit_ltx23.R:270-281).  It is replicated once per lane, entry b of lane l
+// at word b * 32 + l, so 32 lanes looking up arbitrary bytes hit 32 distinct
+// banks.  32 KB.
+constexpr int kNf4LutBytes = 256 * 32 * 4;
+
+// Fill the LUT (called by every thread of the CTA; caller synchronizes).
+__device__ __forceinline__ void nf4_lut_fill(uint32_t* lut) {
+  for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) {
+    const int b = i >> 5;
+    constexpr uint16_t t[16] = {kNf4LevelBits[0],  kNf4LevelBits[1],  kNf4LevelBits[2],
+                                kNf4LevelBits[3],  kNf4LevelBits[4],  kNf4LevelBits[5],
+                                kNf4LevelBits[6],  kNf4LevelBits[7],  kNf4LevelBits[8],
+                                kNf4LevelBits[9],  kNf4LevelBits[10], kNf4LevelBits[11],
+                                kNf4LevelBits[12], kNf4LevelBits[13], kNf4LevelBits[14],
+                                kNf4LevelBits[15]};
+    lut[i] = static_cast<uint32_t>(t[b >> 4]) | (static_cast<uint32_t>(t[b & 15]) << 16);
+  }
+}
+
+// Decode one 32-bit word of packed NF4 through the shared LUT: four
+// conflict-free lookups, each multiplied by the bf16 block scale (sc2, held
+// twice) with one RNE rounding.  lut_lane points at this lane's entry 0
+// (LUT base + lane).
+__device__ __forceinline__ void nf4_decode_word_lut(uint32_t w, const uint32_t* lut_lane,
+                                                    uint32_t sc2, uint32_t* o) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t b = prmt(w, 0u, 0x4440u + i);  // byte i, zero-extended
+    o[i] = bf16x2_mul(lut_lane[b * 32u], sc2);
   }
 }
 

@@ -12,10 +12,19 @@
 //     tensor memory, double-buffered when it fits, and drained by epilogue
 //     warps that add the bias, round to bf16 and store Y row-major.
 // Warp roles (one persistent CTA per SM, static round-robin over tiles):
-//   warps 0-3            epilogue (warp w owns TMEM lanes 32w..32w+31)
-//   warps 4..4+DQ-1      dequant  (warp w writes lanes 32(w%4).., column half (w-4)/4)
-//   warp 4+DQ            producer (TMA for X and packed W; cp.async for absmax)
-//   warp 5+DQ            MMA issuer (one thread) and TMEM allocator
+//   warps 0-3     epilogue (warp w owns TMEM lanes 32w..32w+31)
+//   warps 4-11    dequant, two groups of four; a group decodes every other
+//                 k-block of a round (warp w writes TMEM lanes 32(w%4)..)
+//   warp 12       weight producer (TMA of the packed weight, deep ring)
+//   warp 13       MMA issuer (one thread) and TMEM allocator
+//   warp 14       activation producer (TMA of X tiles)
+// Three rings decouple the operands' lifetimes: packed-weight stages are
+// released as soon as the dequant warps have read them, so the weight ring
+// runs far ahead; X stages and TMEM A stages are released per ROUND by one
+// tcgen05.commit of the MMA thread.  A round is kRound k-blocks: the MMA
+// thread waits once and commits once per round, because a thread that touches
+// shared memory after a tcgen05.commit pays a fixed latency of several hundred
+// cycles, which per-k-block handshakes would add to every 64-deep MMA step.
 // Every mbarrier wait is bounded (dq_ptx.cuh); on expiry the CTA unwinds,
 // drains its in-flight copies and MMAs (bounded), frees TMEM and records
 // DQ_ERR_TIMEOUT in g_dq_error.
@@ -35,6 +44,22 @@ enum : unsigned int { kErrTimeout = 5u };
 // The library is a single translation unit, so it is defined here.
 __device__ unsigned int g_dq_error = 0;
 
+// Optional per-role timestamps (SM clock) of CTA 0, for pipeline analysis.
+// Compiled out unless DQ_TRACE is defined; a tracing build supplies
+// g_dq_trace[slot][index].
+#ifdef DQ_TRACE
+constexpr int kTraceLen = 4096;
+__device__ long long g_dq_trace[16][kTraceLen];
+#define DQ_TRACE_POINT(slot, idx)                                   \
+  do {                                                              \
+    if (blockIdx.x == 0 && (idx) < kTraceLen) g_dq_trace[slot][idx] = clock64(); \
+  } while (0)
+#else
+#define DQ_TRACE_POINT(slot, idx) \
+  do {                            \
+  } while (0)
+#endif
+
 struct GemmArgs {
   const float* absmax;        // NF4: [N, K/64] f32 block scales
   const __nv_bfloat16* bias;  // [N] or nullptr
@@ -50,40 +75,51 @@ template <int FMT, int BM>
 struct GemmCfg {
   static_assert(BM % 16 == 0 && BM >= 16 && BM <= 256, "BM must be a multiple of 16 in [16,256]");
   static constexpr int kBN = 128;                               // weight rows per tile (MMA M)
-  static constexpr int kBK = 64;                                // K per k-block
   static constexpr int kWBytes = FMT == kFmtNF4 ? 32 : 64;      // packed bytes per row per k-block
   static constexpr int kNumAcc = BM <= 192 ? 2 : 1;             // accumulator buffers
   static constexpr int kAccStride = BM < 32 ? 32 : BM;          // TMEM columns per accumulator
   static constexpr int kACol0 = ((kNumAcc * kAccStride + 31) / 32) * 32;
-  static constexpr int kAStagesFit = (512 - kACol0) / 32;
-  static constexpr int kAStages = kAStagesFit > 8 ? 8 : kAStagesFit;
-  static_assert(kAStages >= 2, "not enough TMEM for the A ring");
-  static constexpr int kDqWarps = BM <= 64 ? 8 : 4;
-  static constexpr int kColsPerDqThread = 32 / (kDqWarps / 4);  // TMEM columns per k-block
-  static constexpr int kBytesPerDqThread = kWBytes / (kDqWarps / 4);
-  static constexpr int kProducerWarp = 4 + kDqWarps;
+  // k-blocks per MMA round: enough tensor work per handshake (>= ~512 cycles).
+  static constexpr int kRound = BM >= 256 ? 1 : (BM >= 128 ? 2 : 4);
+  static constexpr int kDqGroups = 2;
+  static constexpr int kDqWarps = 4 * kDqGroups;
+  static constexpr int kWProducerWarp = 4 + kDqWarps;
   static constexpr int kMmaWarp = 5 + kDqWarps;
-  static constexpr int kThreads = (6 + kDqWarps) * 32;
+  static constexpr int kXProducerWarp = 6 + kDqWarps;
+  static constexpr int kThreads = (7 + kDqWarps) * 32;
   static constexpr int kXStageBytes = BM * 128;
   static constexpr int kWStageBytes = kBN * kWBytes;
-  static constexpr int kAmStageBytes = FMT == kFmtNF4 ? kBN * 4 : 0;
-  static constexpr int kStageBytes = kXStageBytes + kWStageBytes + kAmStageBytes;
-  static constexpr int kEpiBytes = 4 * 16 * 32 * 4;             // per-warp 16x32 f32 staging
-  static constexpr int kSmemBudget = 200 * 1024;
-  static constexpr int kStagesFit = (kSmemBudget - kEpiBytes - 1024) / kStageBytes;
-  static constexpr int kStages = kStagesFit > 16 ? 16 : kStagesFit;
-  static_assert(kStages >= 2, "shared memory too small for two stages");
-  static constexpr int kNumBars = 2 * kStages + 2 * kAStages + 2 * kNumAcc + 1;
-  static constexpr int kOffW = kStages * kXStageBytes;
-  static constexpr int kOffAm = kOffW + kStages * kWStageBytes;
-  static constexpr int kOffEpi = kOffAm + kStages * kAmStageBytes;
+  static constexpr int kEpiCols = BM % 32 == 0 ? 32 : 16;       // accumulator columns per drain step
+  static constexpr int kEpiBytes = 4 * kEpiCols * 32 * 4;       // per-warp [cols][32] f32 staging
+  static constexpr int kSmemLimit = 227 * 1024;
+  // NF4 decodes through a 32 KB shared byte LUT (dq_codec.cuh)
+  static constexpr int kLutBytes = FMT == kFmtNF4 ? kNf4LutBytes : 0;
+  // weight ring: 32 KB (NF4) / 48 KB (fp8) of packed tiles
+  static constexpr int kWStages = ((FMT == kFmtNF4 ? 32 : 48) * 1024) / kWStageBytes;
+  // activation ring: rounds of X tiles in the rest
+  static constexpr int kXRoundsFit =
+      (kSmemLimit - kEpiBytes - 2048 - kLutBytes - kWStages * kWStageBytes) / (kRound * kXStageBytes);
+  static constexpr int kXRounds = kXRoundsFit > 4 ? 4 : kXRoundsFit;
+  static_assert(kXRounds >= 2, "need two rounds of X tiles in flight");
+  static constexpr int kXStages = kXRounds * kRound;
+  // TMEM A ring
+  static constexpr int kARoundsFit = (512 - kACol0) / 32 / kRound;
+  static constexpr int kARounds = kARoundsFit > 4 ? 4 : kARoundsFit;
+  static_assert(kARounds >= 2, "need two rounds of TMEM A stages");
+  static constexpr int kAStages = kARounds * kRound;
+  // one completion barrier per round, shared by the X and A rings
+  static constexpr int kDoneBars = kXRounds > kARounds ? kXRounds : kARounds;
+  static constexpr int kNumBars = 2 * kWStages + kXStages + kDoneBars + kARounds + 2 * kNumAcc + 1;
+  static constexpr int kOffW = kXStages * kXStageBytes;
+  static constexpr int kOffLut = kOffW + kWStages * kWStageBytes;
+  static constexpr int kOffEpi = kOffLut + kLutBytes;
   static constexpr int kOffBar = kOffEpi + kEpiBytes;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   // Padded so that one CTA fills an SM: the CTA allocates all 512 TMEM columns.
   static constexpr int kSmemUsed = kOffMisc + 16 + 1024;
   static constexpr int kSmemBytes = kSmemUsed < 120 * 1024 ? 120 * 1024 : kSmemUsed;
+  static_assert(kSmemBytes <= kSmemLimit, "shared memory over the per-CTA limit");
   static constexpr uint32_t kIdesc = make_idesc_bf16(kBN, BM);
-  static constexpr uint32_t kTxBytes = kXStageBytes + kWStageBytes;
 };
 
 struct TileCoord {
@@ -101,45 +137,96 @@ __device__ __forceinline__ TileCoord tile_coord(const GemmArgs& a, int t, int KB
   return c;
 }
 
+// Position in this CTA's sequence of rounds: tile t, first k-block kb of the
+// round (k-blocks kb .. kb+R-1, those >= tc.kb1 are absent).
+struct RoundCursor {
+  int t, kb;
+  TileCoord tc;
+  bool valid;
+};
+
+__device__ __forceinline__ RoundCursor round_begin(const GemmArgs& a, int KB) {
+  RoundCursor c;
+  c.t = blockIdx.x;
+  c.valid = c.t < a.num_tiles;
+  if (c.valid) {
+    c.tc = tile_coord(a, c.t, KB);
+    c.kb = c.tc.kb0;
+  }
+  return c;
+}
+
+template <int R>
+__device__ __forceinline__ void round_advance(RoundCursor& c, const GemmArgs& a, int KB) {
+  if (!c.valid) return;
+  c.kb += R;
+  if (c.kb >= c.tc.kb1) {
+    c.t += gridDim.x;
+    c.valid = c.t < a.num_tiles;
+    if (c.valid) {
+      c.tc = tile_coord(a, c.t, KB);
+      c.kb = c.tc.kb0;
+    }
+  }
+}
+
+// absmax of (row r of the round's tile, k-block kb); 0 when absent.
+__device__ __forceinline__ float load_absmax(const GemmArgs& a, const RoundCursor& c, int kb, int r,
+                                             int KB) {
+  const int n = c.tc.n0 + r;
+  if (!c.valid || n >= a.N || kb >= c.tc.kb1) return 0.f;
+  return __ldg(a.absmax + static_cast<size_t>(n) * KB + kb);
+}
+
 template <int FMT, int BM>
 __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
     dq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x,
                    const __grid_constant__ CUtensorMap tmap_w, const GemmArgs args) {
   using C = GemmCfg<FMT, BM>;
+  constexpr int R = C::kRound;
+  constexpr int XR = C::kXRounds;
+  constexpr int AR = C::kARounds;
+  constexpr int DB = C::kDoneBars;
+  constexpr int WS = C::kWStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + C::kOffBar;
-  // barrier layout: full[S], empty[S], a_full[A], a_empty[A], acc_full[ACC], acc_empty[ACC], drain
-  auto full_bar = [&](int s) { return bar0 + 8u * s; };
-  auto empty_bar = [&](int s) { return bar0 + 8u * (C::kStages + s); };
-  auto afull_bar = [&](int s) { return bar0 + 8u * (2 * C::kStages + s); };
-  auto aempty_bar = [&](int s) { return bar0 + 8u * (2 * C::kStages + C::kAStages + s); };
-  auto accfull_bar = [&](int s) { return bar0 + 8u * (2 * C::kStages + 2 * C::kAStages + s); };
-  auto accempty_bar = [&](int s) {
-    return bar0 + 8u * (2 * C::kStages + 2 * C::kAStages + C::kNumAcc + s);
+  // barriers: wfull[WS], wempty[WS], xfull[XS], done[DB], afull[AR], acc_full, acc_empty, drain
+  auto wfull_bar = [&](int s) { return bar0 + 8u * s; };
+  auto wempty_bar = [&](int s) { return bar0 + 8u * (WS + s); };
+  auto xfull_bar = [&](int s) { return bar0 + 8u * (2 * WS + s); };
+  auto done_bar = [&](int d) { return bar0 + 8u * (2 * WS + C::kXStages + d); };
+  auto afull_bar = [&](int a) { return bar0 + 8u * (2 * WS + C::kXStages + DB + a); };
+  auto accfull_bar = [&](int a) { return bar0 + 8u * (2 * WS + C::kXStages + DB + AR + a); };
+  auto accempty_bar = [&](int a) {
+    return bar0 + 8u * (2 * WS + C::kXStages + DB + AR + C::kNumAcc + a);
   };
   const uint32_t drain_bar = bar0 + 8u * (C::kNumBars - 1);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kOffMisc + 4);
+  // Wait until round qq's MMAs have retired (no wait for qq < 0).
+  auto wait_done = [&](int qq) -> bool {
+    if (qq < 0) return true;
+    return mbar_wait(done_bar(qq % DB), static_cast<uint32_t>((qq / DB) & 1), abort_flag);
+  };
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int KB = (args.K + 63) / 64;  // fp8 allows a ragged last k-block (TMA zero-fills it)
 
-  if (warp == C::kProducerWarp && lane == 0) {
-    for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(full_bar(s), 1);
-      mbar_init(empty_bar(s), 1 + C::kDqWarps);
+  if (warp == C::kWProducerWarp && lane == 0) {
+    for (int s = 0; s < WS; ++s) {
+      mbar_init(wfull_bar(s), 1);
+      mbar_init(wempty_bar(s), 4);  // the four warps of the group that decoded it
     }
-    for (int s = 0; s < C::kAStages; ++s) {
-      mbar_init(afull_bar(s), C::kDqWarps);
-      mbar_init(aempty_bar(s), 1);
-    }
-    for (int s = 0; s < C::kNumAcc; ++s) {
-      mbar_init(accfull_bar(s), 1);
-      mbar_init(accempty_bar(s), 4);
+    for (int s = 0; s < C::kXStages; ++s) mbar_init(xfull_bar(s), 1);
+    for (int d = 0; d < DB; ++d) mbar_init(done_bar(d), 1);
+    for (int a = 0; a < AR; ++a) mbar_init(afull_bar(a), 4 * R);  // four warps per k-block
+    for (int a = 0; a < C::kNumAcc; ++a) {
+      mbar_init(accfull_bar(a), 1);
+      mbar_init(accempty_bar(a), 4);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -151,87 +238,115 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
     tmem_alloc(smem_u32(tmem_holder), 512);
     tmem_relinquish();
   }
+  if constexpr (FMT == kFmtNF4) nf4_lut_fill(reinterpret_cast<uint32_t*>(smem + C::kOffLut));
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
-  if (warp == C::kProducerWarp) {
-    // ------------------------------------------------------------ producer
-    int stage = 0;
-    uint32_t phase = 0;
-    int issued = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; t < args.num_tiles && ok; t += gridDim.x) {
-      const TileCoord tc = tile_coord(args, t, KB);
-      const int m0 = tc.m0 * BM;
-      for (int kb = tc.kb0; kb < tc.kb1; ++kb) {
-        if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) { ok = false; break; }
-        const uint32_t xs = sbase + stage * C::kXStageBytes;
-        const uint32_t ws = sbase + C::kOffW + stage * C::kWStageBytes;
-        if constexpr (FMT == kFmtNF4) {
-          const uint32_t ams = sbase + C::kOffAm + stage * C::kAmStageBytes;
+  if (warp == C::kWProducerWarp) {
+    // ----------------------------------------------------- weight producer
+    if (lane == 0) {
+      int iw = 0;  // running count of present k-blocks = weight ring position
+      for (RoundCursor rc = round_begin(args, KB); rc.valid; round_advance<R>(rc, args, KB)) {
+        for (int j = 0; j < R; ++j) {
+          const int kb = rc.kb + j;
+          if (kb >= rc.tc.kb1) break;
+          const int s = iw % WS;
+          if (!mbar_wait(wempty_bar(s), static_cast<uint32_t>(((iw / WS) & 1) ^ 1), abort_flag)) break;
+          DQ_TRACE_POINT(0, iw);
+          mbar_arrive_expect_tx(wfull_bar(s), C::kWStageBytes);
+          tma_load_2d(sbase + C::kOffW + s * C::kWStageBytes, &tmap_w, wfull_bar(s), kb * C::kWBytes,
+                      rc.tc.n0);
+          ++iw;
+        }
+        if (*abort_flag) break;
+      }
+      if (*abort_flag) {
+        // Let issued copies land before shared memory is released (bounded).
+        for (int i = 1; i <= WS && i <= iw; ++i) {
+          volatile int never = 0;
+          mbar_wait(wfull_bar((iw - i) % WS), static_cast<uint32_t>(((iw - i) / WS) & 1), &never,
+                    100000000ull);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == C::kXProducerWarp) {
+    // ------------------------------------------------- activation producer
+    if (lane == 0) {
+      int q = 0;
+      for (RoundCursor rc = round_begin(args, KB); rc.valid; round_advance<R>(rc, args, KB), ++q) {
+        // X slots of round q were last used by round q - XR.
+        if (!wait_done(q - XR)) break;
+        DQ_TRACE_POINT(1, q);
+        const int m0 = rc.tc.m0 * BM;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int r = lane + 32 * i;
-            const int n = tc.n0 + r;
-            if (n < args.N) cp_async_4(ams + 4u * r, args.absmax + static_cast<size_t>(n) * KB + kb);
+        for (int j = 0; j < R; ++j) {
+          const int slot = (q % XR) * R + j;
+          const int kb = rc.kb + j;
+          if (kb < rc.tc.kb1) {
+            mbar_arrive_expect_tx(xfull_bar(slot), C::kXStageBytes);
+            tma_load_2d(sbase + slot * C::kXStageBytes, &tmap_x, xfull_bar(slot), kb * 64, m0);
+          } else {
+            mbar_arrive(xfull_bar(slot));  // absent k-block: complete the phase with no data
           }
-          cp_async_mbar_arrive(full_bar(stage));
         }
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive_expect_tx(full_bar(stage), C::kTxBytes);
-          tma_load_2d(xs, &tmap_x, full_bar(stage), kb * 64, m0);
-          tma_load_2d(ws, &tmap_w, full_bar(stage), kb * C::kWBytes, tc.n0);
+      }
+      if (*abort_flag) {
+        for (int i = 1; i <= XR && i <= q; ++i) {
+          const int qq = q - i;
+          for (int j = 0; j < R; ++j) {
+            volatile int never = 0;
+            mbar_wait(xfull_bar((qq % XR) * R + j), static_cast<uint32_t>((qq / XR) & 1), &never,
+                      100000000ull);
+          }
         }
-        ++issued;
-        if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
       }
     }
-    if (*abort_flag) {
-      // Let the copies already issued land before the CTA's shared memory is
-      // released (bounded: a copy that never lands is abandoned after 100 ms).
-      int st = stage;
-      uint32_t ph = phase;
-      const int pending = issued < C::kStages ? issued : C::kStages;
-      for (int i = 0; i < pending; ++i) {
-        if (--st < 0) { st = C::kStages - 1; ph ^= 1u; }
-        volatile int never = 0;
-        mbar_wait(full_bar(st), ph, &never, 100000000ull);
-      }
-    }
+    __syncwarp();
   } else if (warp == C::kMmaWarp) {
     // ------------------------------------------------------------------ MMA
     if (lane == 0) {
-      int stage = 0, astage = 0, acc = 0;
-      uint32_t phase = 0, aphase = 0, accphase = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < args.num_tiles && ok; t += gridDim.x) {
-        const TileCoord tc = tile_coord(args, t, KB);
-        if (!mbar_wait(accempty_bar(acc), accphase ^ 1u, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * C::kAccStride);
-        for (int kb = tc.kb0; kb < tc.kb1; ++kb) {
-          if (!mbar_wait(full_bar(stage), phase, abort_flag)) { ok = false; break; }
-          if (!mbar_wait(afull_bar(astage), aphase, abort_flag)) { ok = false; break; }
+      int q = 0, acc = 0;
+      uint32_t accphase = 0;
+      uint32_t d_tmem = 0;
+      for (RoundCursor rc = round_begin(args, KB); rc.valid; ++q) {
+        if (rc.kb == rc.tc.kb0) {
+          if (!mbar_wait(accempty_bar(acc), accphase ^ 1u, abort_flag)) break;
           tc_fence_after();
-          const uint64_t bdesc = make_sw128_kmajor_desc(sbase + stage * C::kXStageBytes);
-          const uint32_t a_tmem = tmem_base + static_cast<uint32_t>(C::kACol0 + astage * 32);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            // K step j: 16 bf16 = 8 TMEM columns of A, 32 bytes along the swizzled B rows.
-            tc_mma_ts(d_tmem, a_tmem + 8u * j, bdesc + static_cast<uint64_t>(2 * j), C::kIdesc,
-                      (kb > tc.kb0 || j > 0) ? 1u : 0u);
-          }
-          tc_commit(empty_bar(stage));
-          tc_commit(aempty_bar(astage));
-          if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
-          if (++astage == C::kAStages) { astage = 0; aphase ^= 1u; }
+          d_tmem = tmem_base + static_cast<uint32_t>(acc * C::kAccStride);
         }
-        if (!ok) break;
-        tc_commit(accfull_bar(acc));
-        if (++acc == C::kNumAcc) { acc = 0; accphase ^= 1u; }
+        // The dequant warps arrive only after observing the round's X tiles
+        // land, so this one wait covers both operands.
+        DQ_TRACE_POINT(2, q);
+        if (!mbar_wait(afull_bar(q % AR), static_cast<uint32_t>((q / AR) & 1), abort_flag)) break;
+        DQ_TRACE_POINT(3, q);
+        tc_fence_after();
+#pragma unroll
+        for (int j = 0; j < R; ++j) {
+          const int kb = rc.kb + j;
+          if (kb < rc.tc.kb1) {
+            const uint64_t bdesc =
+                make_sw128_kmajor_desc(sbase + ((q % XR) * R + j) * C::kXStageBytes);
+            const uint32_t a_tmem =
+                tmem_base + static_cast<uint32_t>(C::kACol0 + ((q % AR) * R + j) * 32);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              // K step k: 16 bf16 = 8 TMEM columns of A, 32 bytes along the swizzled B rows.
+              tc_mma_ts(d_tmem, a_tmem + 8u * k, bdesc + static_cast<uint64_t>(2 * k), C::kIdesc,
+                        (kb > rc.tc.kb0 || k > 0) ? 1u : 0u);
+            }
+          }
+        }
+        tc_commit(done_bar(q % DB));
+        DQ_TRACE_POINT(4, q);
+        const int t_now = rc.t;
+        round_advance<R>(rc, args, KB);
+        if (!rc.valid || rc.t != t_now) {
+          tc_commit(accfull_bar(acc));
+          if (++acc == C::kNumAcc) { acc = 0; accphase ^= 1u; }
+        }
       }
       if (*abort_flag) {
         // Wait (bounded) until every MMA this thread issued has retired.
@@ -245,65 +360,104 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
     // -------------------------------------------------------------- dequant
     const int dw = warp - 4;
     const int quad = warp & 3;           // TMEM lane quadrant this warp may access
-    const int half = dw >> 2;            // which column slice of the k-block
+    const int group = dw >> 2;           // this warp decodes k-blocks j = group, group + G, ...
     const int r = quad * 32 + lane;      // weight row within the tile
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     float sfp8 = 0.f;
     if constexpr (FMT == kFmtFP8) sfp8 = __bfloat162float(__float2bfloat16_rn(args.fp8_scale));
-    int stage = 0, astage = 0;
-    uint32_t phase = 0, aphase = 0;
+    constexpr int G = C::kDqGroups;
+    // k-block j of round q belongs to group (q * R + j) % G, so the groups
+    // alternate k-blocks whatever the round length.
+    auto mine = [&](int qq, int j) { return ((qq * R + j) % G) == group; };
+    RoundCursor rc = round_begin(args, KB);
+    // Block scales are fetched one round ahead of their use.
+    float am[R];
+#pragma unroll
+    for (int j = 0; j < R; ++j)
+      am[j] = (FMT == kFmtNF4 && mine(0, j)) ? load_absmax(args, rc, rc.kb + j, r, KB) : 0.f;
+    int iw = 0;  // weight ring position of the round's first k-block
     bool ok = true;
-    for (int t = blockIdx.x; t < args.num_tiles && ok; t += gridDim.x) {
-      const TileCoord tc = tile_coord(args, t, KB);
-      const bool row_ok = (tc.n0 + r) < args.N;
-      for (int kb = tc.kb0; kb < tc.kb1; ++kb) {
-        if (!mbar_wait(full_bar(stage), phase, abort_flag)) { ok = false; break; }
-        const uint8_t* wrow = smem + C::kOffW + stage * C::kWStageBytes + r * C::kWBytes +
-                              half * C::kBytesPerDqThread;
-        uint4 pk[C::kBytesPerDqThread / 16];
+    for (int q = 0; rc.valid && ok; ++q) {
+      RoundCursor nx = rc;
+      round_advance<R>(nx, args, KB);
+      float am_next[R];
 #pragma unroll
-        for (int i = 0; i < C::kBytesPerDqThread / 16; ++i)
-          pk[i] = *reinterpret_cast<const uint4*>(wrow + 16 * i);
-        float am = 0.f;
-        if constexpr (FMT == kFmtNF4)
-          am = *reinterpret_cast<const float*>(smem + C::kOffAm + stage * C::kAmStageBytes + 4 * r);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty_bar(stage));
-        if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
-
-        uint32_t out[32];
-        const uint32_t* pw = reinterpret_cast<const uint32_t*>(pk);
-        if constexpr (FMT == kFmtNF4) {
-          const uint32_t sc2 = nf4_scale2(am);
+      for (int j = 0; j < R; ++j)
+        am_next[j] = (FMT == kFmtNF4 && mine(q + 1, j)) ? load_absmax(args, nx, nx.kb + j, r, KB) : 0.f;
+      const int present = min(R, rc.tc.kb1 - rc.kb);
+      const bool row_ok = (rc.tc.n0 + r) < args.N;
+      bool tmem_free = false;
 #pragma unroll
-          for (int i = 0; i < C::kBytesPerDqThread / 4; ++i) nf4_decode_word(pw[i], sc2, out + 4 * i);
-        } else {
+      for (int j = 0; j < R; ++j) {
+        if (!mine(q, j)) continue;
+        if (j < present) {
+          const int ws = (iw + j) % WS;
+          if (!mbar_wait(wfull_bar(ws), static_cast<uint32_t>(((iw + j) / WS) & 1), abort_flag)) {
+            ok = false;
+            break;
+          }
+          const bool tp = lane == 0 && quad == 0;
+          if (tp) DQ_TRACE_POINT(5 + 5 * group, q * R + j);
+          const uint4* wrow =
+              reinterpret_cast<const uint4*>(smem + C::kOffW + ws * C::kWStageBytes + r * C::kWBytes);
+          uint4 pk[C::kWBytes / 16];
 #pragma unroll
-          for (int i = 0; i < C::kBytesPerDqThread / 4; ++i) fp8_decode_word(pw[i], sfp8, out + 2 * i);
+          for (int i = 0; i < C::kWBytes / 16; ++i) pk[i] = wrow[i];
+          __syncwarp();
+          if (lane == 0) mbar_arrive(wempty_bar(ws));
+          if (tp && group == 0) DQ_TRACE_POINT(15, q * R + j);
+          uint32_t out[32];
+          const uint32_t* pw = reinterpret_cast<const uint32_t*>(pk);
+          if constexpr (FMT == kFmtNF4) {
+            const uint32_t sc2 = nf4_scale2(am[j]);
+            const uint32_t* lut_lane = reinterpret_cast<const uint32_t*>(smem + C::kOffLut) + lane;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) nf4_decode_word_lut(pw[i], lut_lane, sc2, out + 4 * i);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) fp8_decode_word(pw[i], sfp8, out + 2 * i);
+          }
+          if (!row_ok) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) out[i] = 0u;
+          }
+          if (tp) DQ_TRACE_POINT(6 + 5 * group, q * R + j);
+          // The MMA thread waits only on afull: make sure this k-block's X
+          // tile has landed before vouching for it.
+          if (!mbar_wait(xfull_bar((q % XR) * R + j), static_cast<uint32_t>((q / XR) & 1),
+                         abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (tp) DQ_TRACE_POINT(7 + 5 * group, q * R + j);
+          if (!tmem_free) {
+            // TMEM A stages of this round were last read by round q - AR.
+            if (!wait_done(q - AR)) { ok = false; break; }
+            tc_fence_after();
+            tmem_free = true;
+          }
+          tmem_st_x32(tmem_base + lane_addr +
+                          static_cast<uint32_t>(C::kACol0 + ((q % AR) * R + j) * 32),
+                      out);
+          tmem_wait_st();
+          tc_fence_before();
+          if (tp) DQ_TRACE_POINT(8 + 5 * group, q * R + j);
         }
-        if (!row_ok) {
-#pragma unroll
-          for (int i = 0; i < C::kColsPerDqThread; ++i) out[i] = 0u;
-        }
-        if (!mbar_wait(aempty_bar(astage), aphase ^ 1u, abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t a_addr = tmem_base + lane_addr +
-                                static_cast<uint32_t>(C::kACol0 + astage * 32 + half * C::kColsPerDqThread);
-#pragma unroll
-        for (int c = 0; c < C::kColsPerDqThread / 16; ++c)
-          tmem_st_x16(a_addr + 16u * c, *reinterpret_cast<const uint32_t(*)[16]>(out + 16 * c));
-        tmem_wait_st();
-        tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(afull_bar(astage));
-        if (++astage == C::kAStages) { astage = 0; aphase ^= 1u; }
+        if (lane == 0) mbar_arrive(afull_bar(q % AR));
+        if (lane == 0 && quad == 0) DQ_TRACE_POINT(9 + 5 * group, q * R + j);
       }
+#pragma unroll
+      for (int j = 0; j < R; ++j) am[j] = am_next[j];
+      iw += present;
+      rc = nx;
     }
   } else {
     // ------------------------------------------------------------- epilogue
+    constexpr int EC = C::kEpiCols;
     const int quad = warp;  // warps 0..3
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
-    uint8_t* stg = smem + C::kOffEpi + quad * (16 * 32 * 4);
+    uint8_t* stg = smem + C::kOffEpi + quad * (EC * 32 * 4);
     int acc = 0;
     uint32_t accphase = 0;
     const bool f32_out = args.splits > 1;
@@ -316,29 +470,42 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
       if (!mbar_wait(accfull_bar(acc), accphase, abort_flag)) break;
       tc_fence_after();
       const uint32_t d_addr = tmem_base + lane_addr + static_cast<uint32_t>(acc * C::kAccStride);
-#pragma unroll 1
-      for (int c = 0; c < BM / 16; ++c) {
-        uint32_t v[16];
-        tmem_ld_x16(d_addr + 16u * c, v);
+      const int ncol0 = tc.n0 + quad * 32;
+      constexpr int NC = BM / EC;
+      // Double-buffered drain: the TMEM load of chunk c+1 is in flight while
+      // chunk c is converted and stored.
+      uint32_t v[2][32];
+      auto tmem_load = [&](int c, uint32_t* dst) {
+        if constexpr (EC == 32) {
+          tmem_ld_x32(d_addr + 32u * c, dst);
+        } else {
+          tmem_ld_x16(d_addr + 16u * c, *reinterpret_cast<uint32_t(*)[16]>(dst));
+        }
+      };
+      tmem_load(0, v[0]);
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
         tmem_wait_ld();
-        if (c == BM / 16 - 1) {
+        if (c + 1 < NC) {
+          tmem_load(c + 1, v[(c + 1) & 1]);
+        } else {
           // The whole accumulator has been read: hand it back to the MMA warp.
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(accempty_bar(acc));
         }
-        const int mrow0 = m0 + 16 * c;  // token of staging row 0
-        const int ncol0 = tc.n0 + quad * 32;
+        const uint32_t* vc = v[c & 1];
+        const int mrow0 = m0 + EC * c;  // token of staging row 0
         if (!f32_out) {
-          // stage [16 tokens][32 outputs] bf16, then write 64-byte row segments
+          // stage [EC tokens][32 outputs] bf16, then write 64-byte row segments
           __nv_bfloat16* sb = reinterpret_cast<__nv_bfloat16*>(stg);
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            sb[j * 32 + lane] = __float2bfloat16_rn(__uint_as_float(v[j]) + bias);
+          for (int j = 0; j < EC; ++j)
+            sb[j * 32 + lane] = __float2bfloat16_rn(__uint_as_float(vc[j]) + bias);
           __syncwarp();
           __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(args.out);
 #pragma unroll
-          for (int i = 0; i < 2; ++i) {
+          for (int i = 0; i < EC / 8; ++i) {
             const int row = (lane >> 2) + 8 * i;
             const int col = (lane & 3) * 8;
             const int m = mrow0 + row;
@@ -356,15 +523,15 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
           }
           __syncwarp();
         } else {
-          // split-K partial: stage [16][32] f32, write 128-byte row segments
+          // split-K partial: stage [EC][32] f32, write 128-byte row segments
           float* sf = reinterpret_cast<float*>(stg);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) sf[j * 32 + lane] = __uint_as_float(v[j]);
+          for (int j = 0; j < EC; ++j) sf[j * 32 + lane] = __uint_as_float(vc[j]);
           __syncwarp();
           float* part = reinterpret_cast<float*>(args.out) +
                         static_cast<size_t>(tc.split) * args.M * args.N;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
+          for (int i = 0; i < EC / 4; ++i) {
             const int row = (lane >> 3) + 4 * i;
             const int col = (lane & 7) * 4;
             const int m = mrow0 + row;
