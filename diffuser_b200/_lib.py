@@ -28,12 +28,16 @@ SIGNATURES = {
                                      _c_p, _c_sz, _c_p]),
     "dq_linear_fp8": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_p, ctypes.c_float, _c_p, _c_i64,
                                      _c_p, _c_p, _c_sz, _c_p]),
+    "dq_linear_nf4_noalloc": (ctypes.c_int, [_c_p, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_i64,
+                                             _c_p, _c_p]),
     "dq_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), _c_p]),
     "dq_set_tile_override": (ctypes.c_int, [ctypes.c_int, ctypes.c_int]),
 }
 
 DQ_OK = 0
 DQ_ERR_TIMEOUT = 5
+DQ_ERR_SCRATCH_LIMIT = 9
+DQ_NOALLOC_SCRATCH_BYTES = 8 << 20
 DQ_FMT_NF4, DQ_FMT_FP8 = 0, 1
 DQ_DTYPE_F32, DQ_DTYPE_BF16 = 0, 1
 

@@ -384,6 +384,8 @@ const char* dq_status_string(int s) {
     case DQ_ERR_WORKSPACE: return "workspace missing or too small";
     case DQ_ERR_ARG: return "null operand or unknown enum";
     case DQ_ERR_CUDA: return "CUDA runtime error";
+    case DQ_ERR_SCRATCH_LIMIT:
+      return "shape needs more split-K scratch than the allocation-free entry point holds (8 MiB)";
   }
   return "unknown status";
 }
@@ -482,6 +484,46 @@ int dq_linear_fp8(const void* x, int64_t M, int64_t K, const uint8_t* w8, float 
                   dq_stream_t stream) {
   return linear_impl(kFmtFP8, x, M, K, w8, nullptr, scale, bias, N, y, workspace, workspace_bytes,
                      static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"
+
+namespace dq {
+// Built-in split-K scratch of dq_linear_nf4_noalloc.  In host code the symbol
+// is only a stand-in: kernels receive the device address that
+// cudaGetSymbolAddress returns for the current device.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[DQ_NOALLOC_SCRATCH_BYTES];
+static std::atomic<void*> g_noalloc_addr[kMaxDevices];
+static std::mutex g_noalloc_mu;
+}  // namespace dq
+
+extern "C" {
+
+int dq_linear_nf4_noalloc(const void* x, int64_t M, int64_t K, const uint8_t* packed,
+                          const float* absmax, const void* bias, int64_t N, void* y,
+                          dq_stream_t stream) {
+  if (M < 0 || N <= 0 || K <= 0 || (K % 64) != 0) return DQ_ERR_SHAPE;
+  if (M == 0) return DQ_OK;
+  DeviceInfo* d = nullptr;
+  int rc = current_device(&d);
+  if (rc != DQ_OK) return rc;
+  if (make_plan(M, N, K, d->sms).ws > DQ_NOALLOC_SCRATCH_BYTES) return DQ_ERR_SCRATCH_LIMIT;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return DQ_ERR_CUDA;
+  void* scratch = g_noalloc_addr[dev].load();
+  if (scratch == nullptr) {
+    // First call on this device (with it current): look up the array's
+    // device address once.
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    scratch = g_noalloc_addr[dev].load();
+    if (scratch == nullptr) {
+      if (cudaGetSymbolAddress(&scratch, g_noalloc_scratch) != cudaSuccess || scratch == nullptr)
+        return DQ_ERR_CUDA;
+      g_noalloc_addr[dev].store(scratch);
+    }
+  }
+  return linear_impl(kFmtNF4, x, M, K, packed, absmax, 0.f, bias, N, y, scratch,
+                     DQ_NOALLOC_SCRATCH_BYTES, static_cast<cudaStream_t>(stream));
 }
 
 int dq_device_error(int* code, dq_stream_t stream) {

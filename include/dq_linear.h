@@ -40,7 +40,8 @@ typedef enum dq_status {
   DQ_ERR_TIMEOUT = 5,   /* a kernel's bounded wait expired (dq_device_error) */
   DQ_ERR_WORKSPACE = 6, /* workspace NULL or smaller than dq_workspace_size() */
   DQ_ERR_ARG = 7,       /* NULL operand pointer or unknown enum value */
-  DQ_ERR_CUDA = 8       /* another CUDA runtime error */
+  DQ_ERR_CUDA = 8,      /* another CUDA runtime error */
+  DQ_ERR_SCRATCH_LIMIT = 9 /* dq_linear_nf4_noalloc: shape needs more scratch than it has */
 } dq_status;
 
 typedef enum dq_format { DQ_FMT_NF4 = 0, DQ_FMT_FP8 = 1 } dq_format;
@@ -99,6 +100,25 @@ int dq_linear_fp8(const void* x, int64_t M, int64_t K,
                   const uint8_t* w8, float scale,
                   const void* bias, int64_t N, void* y,
                   void* workspace, size_t workspace_bytes, dq_stream_t stream);
+
+/* Allocation-free NF4 linear, for callers that cannot allocate device
+ * memory: code running inside a CUDA graph capture or another runtime's
+ * stream callbacks, and embedders whose device memory is owned by a foreign
+ * allocator (the R torch package's caching allocator, for instance) and who
+ * have no workspace to lend.  This entry point has no counterpart in the
+ * reference.  Same math and arguments as dq_linear_nf4 minus the workspace:
+ * split-K partial sums go to a scratch array built into the library
+ * (DQ_NOALLOC_SCRATCH_BYTES = 8 MiB, held on every GPU that loads the
+ * library until the process exits).  A shape whose split-K plan needs more
+ * returns DQ_ERR_SCRATCH_LIMIT without launching anything.  The first call
+ * on a device looks up the array's device address (make that first call
+ * before any stream capture).  All calls share the one array: calls whose
+ * kernels overlap on the GPU (different streams, no ordering) race on it.
+ * Every partial sum is written before it is read, so nothing needs clearing. */
+#define DQ_NOALLOC_SCRATCH_BYTES (8u << 20)
+int dq_linear_nf4_noalloc(const void* x, int64_t M, int64_t K,
+                          const uint8_t* packed, const float* absmax,
+                          const void* bias, int64_t N, void* y, dq_stream_t stream);
 
 /* ---------------------------------------------------------------- errors
  * Reads and clears the current device's kernel error word (synchronizes
