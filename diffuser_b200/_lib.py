@@ -32,6 +32,7 @@ SIGNATURES = {
                                              _c_p, _c_p]),
     "dq_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), _c_p]),
     "dq_set_tile_override": (ctypes.c_int, [ctypes.c_int, ctypes.c_int]),
+    "dq_set_pair_mode": (ctypes.c_int, [ctypes.c_int]),
 }
 
 DQ_OK = 0

@@ -13,6 +13,7 @@
 
 #include "../../include/dq_linear.h"
 #include "dq_gemm.cuh"
+#include "dq_gemm2.cuh"
 
 #define DQ_VERSION_STRING "dqlinear-b200 0.1.0 (sm_100a)"
 
@@ -144,12 +145,14 @@ struct DeviceInfo {
   int ok = 0;  // 1 = probed
   int major = 0, minor = 0, sms = 0;
   int smem_set[2][6] = {};
+  int smem_set2[2][6] = {};
+  int max_pairs[2][6] = {};
 };
 
 constexpr int kMaxDevices = 64;
 static DeviceInfo g_dev[kMaxDevices];
 static std::mutex g_dev_mu;
-static std::atomic<int> g_override_bm{0}, g_override_splits{0};
+static std::atomic<int> g_override_bm{0}, g_override_splits{0}, g_override_pair{0};
 
 static int current_device(DeviceInfo** out) {
   int dev = 0;
@@ -201,6 +204,7 @@ static bool make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType 
 
 // ----------------------------------------------------------- launch plan
 struct Plan {
+  bool pair = false;  // CTA-pair kernel (256 weight rows per tile)
   int bm = 0, splits = 1, kb_per_split = 0;
   int m_tiles = 0, n_tiles = 0, tiles = 0, grid = 0;
   size_t ws = 0;
@@ -221,10 +225,17 @@ static int bm_index(int bm) {
 static Plan make_plan(int64_t M, int64_t N, int64_t K, int sms) {
   Plan p;
   const int KB = static_cast<int>((K + 63) / 64);
-  p.n_tiles = static_cast<int>((N + 127) / 128);
+  // CTA-pair tiles only on request (dq_set_pair_mode) until they beat the
+  // one-CTA kernel.
+  const int opair = g_override_pair.load();
+  p.pair = opair == 2 && M > 64;
+  p.n_tiles = static_cast<int>((N + (p.pair ? 255 : 127)) / (p.pair ? 256 : 128));
+  const int units = p.pair ? sms / 2 : sms;  // concurrently resident tile workers
   const int obm = g_override_bm.load();
-  if (obm > 0 && bm_index(obm) >= 0) {
+  if (obm > 0 && bm_index(obm) >= 0 && (!p.pair || obm >= 64)) {
     p.bm = obm;
+  } else if (p.pair) {
+    p.bm = 0;
   } else if (M <= 16) {
     p.bm = 16;
   } else if (M <= 32) {
@@ -233,7 +244,8 @@ static Plan make_plan(int64_t M, int64_t N, int64_t K, int sms) {
     p.bm = 64;
   } else if (M <= 128) {
     p.bm = 128;
-  } else {
+  }
+  if (p.bm == 0) {
     // Pick the x-tile height that minimizes (waves x tile time); 256 has a
     // single accumulator buffer, so its epilogue does not overlap the MMAs.
     const int cands[3] = {128, 192, 256};
@@ -241,7 +253,7 @@ static Plan make_plan(int64_t M, int64_t N, int64_t K, int sms) {
     double best = 1e30;
     for (int i = 0; i < 3; ++i) {
       const int64_t tiles = ((M + cands[i] - 1) / cands[i]) * p.n_tiles;
-      const double waves = static_cast<double>((tiles + sms - 1) / sms);
+      const double waves = static_cast<double>((tiles + units - 1) / units);
       const double cost = waves * cands[i] * penalty[i];
       if (cost < best - 1e-9) { best = cost; p.bm = cands[i]; }
     }
@@ -252,14 +264,14 @@ static Plan make_plan(int64_t M, int64_t N, int64_t K, int sms) {
   const int os = g_override_splits.load();
   if (os > 0) {
     s = os;
-  } else if (base_tiles * 2 <= sms && KB >= 8) {
-    s = std::min(std::min(sms / base_tiles, KB / 4), 16);
+  } else if (base_tiles * 2 <= units && KB >= 8) {
+    s = std::min(std::min(units / base_tiles, KB / 4), 16);
   }
   s = std::max(1, std::min(s, KB));
   p.kb_per_split = (KB + s - 1) / s;
   p.splits = (KB + p.kb_per_split - 1) / p.kb_per_split;
   p.tiles = base_tiles * p.splits;
-  p.grid = std::min(p.tiles, sms);
+  p.grid = std::min(p.tiles, units);  // CTAs (1-CTA kernel) or pairs (pair kernel)
   p.ws = p.splits > 1 ? static_cast<size_t>(p.splits) * M * N * sizeof(float) : 0;
   return p;
 }
@@ -280,9 +292,52 @@ static int launch_gemm(DeviceInfo* d, const Plan& p, const CUtensorMap& mx, cons
   return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
 }
 
+template <int FMT, int BM>
+static int launch_gemm2(DeviceInfo* d, const Plan& p, const CUtensorMap& mx, const CUtensorMap& mw,
+                        const GemmArgs& a, cudaStream_t st) {
+  using C = Gemm2Cfg<FMT, BM>;
+  auto kern = dq_gemm2_kernel<FMT, BM>;
+  const int bi = bm_index(BM);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (!d->smem_set2[FMT][bi]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
+        cudaSuccess)
+      return DQ_ERR_LAUNCH;
+    int clusters = 0;
+    cfg.gridDim = dim3(2 * std::max(1, d->sms / 2));
+    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1)
+      return DQ_ERR_LAUNCH;
+    d->max_pairs[FMT][bi] = clusters;
+    d->smem_set2[FMT][bi] = 1;
+  }
+  const int pairs = std::max(1, std::min(p.grid, d->max_pairs[FMT][bi]));
+  cfg.gridDim = dim3(2 * pairs);
+  if (cudaLaunchKernelEx(&cfg, kern, mx, mw, a) != cudaSuccess) return DQ_ERR_LAUNCH;
+  return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
+}
+
 template <int FMT>
 static int dispatch_gemm(DeviceInfo* d, const Plan& p, const CUtensorMap& mx, const CUtensorMap& mw,
                          const GemmArgs& a, cudaStream_t st) {
+  if (p.pair) {
+    switch (p.bm) {
+      case 64: return launch_gemm2<FMT, 64>(d, p, mx, mw, a, st);
+      case 128: return launch_gemm2<FMT, 128>(d, p, mx, mw, a, st);
+      case 192: return launch_gemm2<FMT, 192>(d, p, mx, mw, a, st);
+      case 256: return launch_gemm2<FMT, 256>(d, p, mx, mw, a, st);
+    }
+    return DQ_ERR_ARG;
+  }
   switch (p.bm) {
     case 16: return launch_gemm<FMT, 16>(d, p, mx, mw, a, st);
     case 32: return launch_gemm<FMT, 32>(d, p, mx, mw, a, st);
@@ -324,8 +379,8 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
   if (p.ws > 0 && (ws == nullptr || ws_bytes < p.ws || !aligned(ws, 16))) return DQ_ERR_WORKSPACE;
 
   CUtensorMap mx, mw;
-  if (!make_map_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, M, K * 2, 64, p.bm,
-                   CU_TENSOR_MAP_SWIZZLE_128B))
+  if (!make_map_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, M, K * 2, 64,
+                   p.pair ? p.bm / 2 : p.bm, CU_TENSOR_MAP_SWIZZLE_128B))
     return DQ_ERR_CUDA;
   const uint64_t wrow = fmt == kFmtNF4 ? K / 2 : K;
   if (!make_map_2d(&mw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, wrow, N, wrow,
@@ -339,6 +394,7 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
   a.N = static_cast<int>(N);
   a.K = static_cast<int>(K);
   a.num_n_tiles = p.n_tiles;
+  a.tile_n = p.pair ? 256 : 128;
   a.num_tiles = p.tiles;
   a.splits = p.splits;
   a.kb_per_split = p.kb_per_split;
@@ -536,6 +592,12 @@ int dq_device_error(int* code, dq_stream_t stream) {
   const unsigned int zero = 0;
   if (v != 0 && cudaMemcpyToSymbol(g_dq_error, &zero, sizeof(zero)) != cudaSuccess) return DQ_ERR_CUDA;
   *code = (v & (1u << kErrTimeout)) ? DQ_ERR_TIMEOUT : DQ_OK;
+  return DQ_OK;
+}
+
+int dq_set_pair_mode(int mode) {
+  if (mode < 0 || mode > 2) return DQ_ERR_ARG;
+  g_override_pair.store(mode);
   return DQ_OK;
 }
 

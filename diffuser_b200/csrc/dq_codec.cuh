@@ -15,6 +15,8 @@
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
 
+#include "dq_ptx.cuh"
+
 namespace dq {
 
 // bf16 bit patterns of the 16 NF4 levels of R/nf4_ltx23.R:15-21
@@ -129,14 +131,14 @@ __device__ __forceinline__ void nf4_lut_fill(uint32_t* lut) {
 
 // Decode one 32-bit word of packed NF4 through the shared LUT: four
 // conflict-free lookups, each multiplied by the bf16 block scale (sc2, held
-// twice) with one RNE rounding.  lut_lane points at this lane's entry 0
-// (LUT base + lane).
-__device__ __forceinline__ void nf4_decode_word_lut(uint32_t w, const uint32_t* lut_lane,
-                                                    uint32_t sc2, uint32_t* o) {
+// twice) with one RNE rounding.  lut_lane = shared-window address of this
+// lane's entry 0 (LUT base + 4 * lane); entry b is 128 bytes further per b.
+__device__ __forceinline__ void nf4_decode_word_lut(uint32_t w, uint32_t lut_lane, uint32_t sc2,
+                                                    uint32_t* o) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const uint32_t b = prmt(w, 0u, 0x4440u + i);  // byte i, zero-extended
-    o[i] = bf16x2_mul(lut_lane[b * 32u], sc2);
+    o[i] = bf16x2_mul(lds32(lut_lane + b * 128u), sc2);
   }
 }
 

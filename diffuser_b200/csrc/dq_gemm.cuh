@@ -66,6 +66,7 @@ struct GemmArgs {
   void* out;                  // bf16 Y [M, N] (splits == 1) or f32 partials [splits, M, N]
   int M, N, K;
   int num_n_tiles, num_tiles;
+  int tile_n;                 // weight rows per tile: 128 (one CTA) or 256 (CTA pair)
   int splits, kb_per_split;
   float fp8_scale;            // fp8: per-tensor scale (rounded to bf16 in-kernel)
   int vec_ok;                 // 16-byte vector stores are aligned for `out`
@@ -130,7 +131,7 @@ __device__ __forceinline__ TileCoord tile_coord(const GemmArgs& a, int t, int KB
   TileCoord c;
   c.split = t % a.splits;
   const int mn = t / a.splits;
-  c.n0 = (mn % a.num_n_tiles) * 128;
+  c.n0 = (mn % a.num_n_tiles) * a.tile_n;
   c.m0 = (mn / a.num_n_tiles);
   c.kb0 = c.split * a.kb_per_split;
   c.kb1 = min(KB, c.kb0 + a.kb_per_split);
@@ -140,14 +141,17 @@ __device__ __forceinline__ TileCoord tile_coord(const GemmArgs& a, int t, int KB
 // Position in this CTA's sequence of rounds: tile t, first k-block kb of the
 // round (k-blocks kb .. kb+R-1, those >= tc.kb1 are absent).
 struct RoundCursor {
-  int t, kb;
+  int t, kb, stride;
   TileCoord tc;
   bool valid;
 };
 
-__device__ __forceinline__ RoundCursor round_begin(const GemmArgs& a, int KB) {
+// Tiles first, first + stride, ... belong to this CTA (or CTA pair).
+__device__ __forceinline__ RoundCursor round_begin(const GemmArgs& a, int KB, int first,
+                                                   int stride) {
   RoundCursor c;
-  c.t = blockIdx.x;
+  c.t = first;
+  c.stride = stride;
   c.valid = c.t < a.num_tiles;
   if (c.valid) {
     c.tc = tile_coord(a, c.t, KB);
@@ -161,7 +165,7 @@ __device__ __forceinline__ void round_advance(RoundCursor& c, const GemmArgs& a,
   if (!c.valid) return;
   c.kb += R;
   if (c.kb >= c.tc.kb1) {
-    c.t += gridDim.x;
+    c.t += c.stride;
     c.valid = c.t < a.num_tiles;
     if (c.valid) {
       c.tc = tile_coord(a, c.t, KB);
@@ -248,7 +252,7 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
     // ----------------------------------------------------- weight producer
     if (lane == 0) {
       int iw = 0;  // running count of present k-blocks = weight ring position
-      for (RoundCursor rc = round_begin(args, KB); rc.valid; round_advance<R>(rc, args, KB)) {
+      for (RoundCursor rc = round_begin(args, KB, blockIdx.x, gridDim.x); rc.valid; round_advance<R>(rc, args, KB)) {
         for (int j = 0; j < R; ++j) {
           const int kb = rc.kb + j;
           if (kb >= rc.tc.kb1) break;
@@ -276,7 +280,7 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
     // ------------------------------------------------- activation producer
     if (lane == 0) {
       int q = 0;
-      for (RoundCursor rc = round_begin(args, KB); rc.valid; round_advance<R>(rc, args, KB), ++q) {
+      for (RoundCursor rc = round_begin(args, KB, blockIdx.x, gridDim.x); rc.valid; round_advance<R>(rc, args, KB), ++q) {
         // X slots of round q were last used by round q - XR.
         if (!wait_done(q - XR)) break;
         DQ_TRACE_POINT(1, q);
@@ -311,7 +315,7 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
       int q = 0, acc = 0;
       uint32_t accphase = 0;
       uint32_t d_tmem = 0;
-      for (RoundCursor rc = round_begin(args, KB); rc.valid; ++q) {
+      for (RoundCursor rc = round_begin(args, KB, blockIdx.x, gridDim.x); rc.valid; ++q) {
         if (rc.kb == rc.tc.kb0) {
           if (!mbar_wait(accempty_bar(acc), accphase ^ 1u, abort_flag)) break;
           tc_fence_after();
@@ -369,7 +373,7 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
     // k-block j of round q belongs to group (q * R + j) % G, so the groups
     // alternate k-blocks whatever the round length.
     auto mine = [&](int qq, int j) { return ((qq * R + j) % G) == group; };
-    RoundCursor rc = round_begin(args, KB);
+    RoundCursor rc = round_begin(args, KB, blockIdx.x, gridDim.x);
     // Block scales are fetched one round ahead of their use.
     float am[R];
 #pragma unroll
@@ -398,11 +402,12 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
           }
           const bool tp = lane == 0 && quad == 0;
           if (tp) DQ_TRACE_POINT(5 + 5 * group, q * R + j);
-          const uint4* wrow =
-              reinterpret_cast<const uint4*>(smem + C::kOffW + ws * C::kWStageBytes + r * C::kWBytes);
+          const uint32_t wrow = sbase + C::kOffW + ws * C::kWStageBytes + r * C::kWBytes;
           uint4 pk[C::kWBytes / 16];
 #pragma unroll
-          for (int i = 0; i < C::kWBytes / 16; ++i) pk[i] = wrow[i];
+          for (int i = 0; i < C::kWBytes / 16; ++i) pk[i] = lds128(wrow + 16u * i);
+          // the producer's next TMA into this stage must not overtake these reads
+          fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) mbar_arrive(wempty_bar(ws));
           if (tp && group == 0) DQ_TRACE_POINT(15, q * R + j);
@@ -410,7 +415,7 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
           const uint32_t* pw = reinterpret_cast<const uint32_t*>(pk);
           if constexpr (FMT == kFmtNF4) {
             const uint32_t sc2 = nf4_scale2(am[j]);
-            const uint32_t* lut_lane = reinterpret_cast<const uint32_t*>(smem + C::kOffLut) + lane;
+            const uint32_t lut_lane = sbase + C::kOffLut + 4u * lane;
 #pragma unroll
             for (int i = 0; i < 8; ++i) nf4_decode_word_lut(pw[i], lut_lane, sc2, out + 4 * i);
           } else {
@@ -458,6 +463,7 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
     const int quad = warp;  // warps 0..3
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     uint8_t* stg = smem + C::kOffEpi + quad * (EC * 32 * 4);
+    const uint32_t stg_s = sbase + C::kOffEpi + quad * (EC * 32 * 4);
     int acc = 0;
     uint32_t accphase = 0;
     const bool f32_out = args.splits > 1;
@@ -501,7 +507,8 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
           __nv_bfloat16* sb = reinterpret_cast<__nv_bfloat16*>(stg);
 #pragma unroll
           for (int j = 0; j < EC; ++j)
-            sb[j * 32 + lane] = __float2bfloat16_rn(__uint_as_float(vc[j]) + bias);
+            sts16(stg_s + 2u * (j * 32 + lane),
+                  __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(vc[j]) + bias)));
           __syncwarp();
           __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(args.out);
 #pragma unroll
@@ -514,7 +521,7 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
               __nv_bfloat16* dst = y + static_cast<size_t>(m) * args.N + nc;
               const __nv_bfloat16* src = sb + row * 32 + col;
               if (args.vec_ok && nc + 8 <= args.N) {
-                *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+                *reinterpret_cast<uint4*>(dst) = lds128(stg_s + 2u * (row * 32 + col));
               } else {
                 for (int e = 0; e < 8; ++e)
                   if (nc + e < args.N) dst[e] = src[e];
@@ -526,7 +533,7 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
           // split-K partial: stage [EC][32] f32, write 128-byte row segments
           float* sf = reinterpret_cast<float*>(stg);
 #pragma unroll
-          for (int j = 0; j < EC; ++j) sf[j * 32 + lane] = __uint_as_float(vc[j]);
+          for (int j = 0; j < EC; ++j) sts32(stg_s + 4u * (j * 32 + lane), vc[j]);
           __syncwarp();
           float* part = reinterpret_cast<float*>(args.out) +
                         static_cast<size_t>(tc.split) * args.M * args.N;
@@ -540,7 +547,8 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
               float* dst = part + static_cast<size_t>(m) * args.N + nc;
               const float* src = sf + row * 32 + col;
               if (args.vec_ok && nc + 4 <= args.N) {
-                *reinterpret_cast<float4*>(dst) = *reinterpret_cast<const float4*>(src);
+                const uint4 q4 = lds128(stg_s + 4u * (row * 32 + col));
+                *reinterpret_cast<uint4*>(dst) = q4;
               } else {
                 for (int e = 0; e < 4; ++e)
                   if (nc + e < args.N) dst[e] = src[e];

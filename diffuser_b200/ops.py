@@ -218,6 +218,11 @@ def device_error(device=None) -> int:
     return code.value
 
 
+def set_pair_mode(mode: int = 0) -> None:
+    """0 = automatic, 1 = one CTA per 128-row tile, 2 = CTA pairs (256-row tiles)."""
+    _lib.check("dq_set_pair_mode", _lib.lib().dq_set_pair_mode(int(mode)))
+
+
 def set_tile_override(bm: int = 0, splits: int = 0) -> None:
     """Force the x-tile height / split-K count (0 = automatic); for sweeps."""
     _lib.check("dq_set_tile_override", _lib.lib().dq_set_tile_override(int(bm), int(splits)))

@@ -129,6 +129,10 @@ int dq_device_error(int* code, dq_stream_t stream);
  * (16..256, multiple of 16; 0 = automatic) and split-K count (0 = auto). */
 int dq_set_tile_override(int bm, int splits);
 
+/* Kernel-family override for benchmarking: 0 = automatic, 1 = one CTA per
+ * tile (128 weight rows), 2 = CTA-pair tiles (256 weight rows, x-tile >= 64). */
+int dq_set_pair_mode(int mode);
+
 #ifdef __cplusplus
 }
 #endif
