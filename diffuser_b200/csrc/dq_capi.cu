@@ -222,20 +222,28 @@ static int bm_index(int bm) {
   return -1;
 }
 
+// Relative per-SM throughput of each large-M tile shape (one-CTA BM=192 = 1),
+// measured on B200 at x[4608,3072] . W[12288,3072]^T for both formats.
+struct TileShape {
+  bool pair;
+  int bm;
+  double eff;
+};
+static constexpr TileShape kShapes[] = {
+    {false, 128, 0.72}, {false, 192, 1.0}, {false, 256, 0.97}, {true, 192, 0.93}, {true, 256, 1.13}};
+
 static Plan make_plan(int64_t M, int64_t N, int64_t K, int sms) {
   Plan p;
   const int KB = static_cast<int>((K + 63) / 64);
-  // CTA-pair tiles only on request (dq_set_pair_mode) until they beat the
-  // one-CTA kernel.
-  const int opair = g_override_pair.load();
-  p.pair = opair == 2 && M > 64;
-  p.n_tiles = static_cast<int>((N + (p.pair ? 255 : 127)) / (p.pair ? 256 : 128));
-  const int units = p.pair ? sms / 2 : sms;  // concurrently resident tile workers
+  const int opair = g_override_pair.load();  // 0 automatic, 1 one-CTA only, 2 pairs only
   const int obm = g_override_bm.load();
-  if (obm > 0 && bm_index(obm) >= 0 && (!p.pair || obm >= 64)) {
+  auto units_of = [&](bool pair) { return pair ? sms / 2 : sms; };
+  auto n_tiles_of = [&](bool pair) { return static_cast<int>((N + (pair ? 255 : 127)) / (pair ? 256 : 128)); };
+  if (opair == 2 && M > 64) {
+    p.pair = true;
+    p.bm = (obm >= 64 && bm_index(obm) >= 0) ? obm : 256;
+  } else if (obm > 0 && bm_index(obm) >= 0) {
     p.bm = obm;
-  } else if (p.pair) {
-    p.bm = 0;
   } else if (M <= 16) {
     p.bm = 16;
   } else if (M <= 32) {
@@ -244,20 +252,26 @@ static Plan make_plan(int64_t M, int64_t N, int64_t K, int sms) {
     p.bm = 64;
   } else if (M <= 128) {
     p.bm = 128;
-  }
-  if (p.bm == 0) {
-    // Pick the x-tile height that minimizes (waves x tile time); 256 has a
-    // single accumulator buffer, so its epilogue does not overlap the MMAs.
-    const int cands[3] = {128, 192, 256};
-    const double penalty[3] = {1.06, 1.0, 1.08};
+  } else {
+    // Minimize waves x tile time over the large-M shapes; CTA-pair shapes only
+    // when they fill every SM pair without split-K.
     double best = 1e30;
-    for (int i = 0; i < 3; ++i) {
-      const int64_t tiles = ((M + cands[i] - 1) / cands[i]) * p.n_tiles;
+    for (const TileShape& c : kShapes) {
+      if (c.pair && opair == 1) continue;
+      const int64_t tiles = ((M + c.bm - 1) / c.bm) * n_tiles_of(c.pair);
+      const int units = units_of(c.pair);
+      if (c.pair && tiles < units) continue;
       const double waves = static_cast<double>((tiles + units - 1) / units);
-      const double cost = waves * cands[i] * penalty[i];
-      if (cost < best - 1e-9) { best = cost; p.bm = cands[i]; }
+      const double cost = waves * (c.pair ? 256.0 : 128.0) * c.bm / ((c.pair ? 2.0 : 1.0) * c.eff);
+      if (cost < best - 1e-9) {
+        best = cost;
+        p.pair = c.pair;
+        p.bm = c.bm;
+      }
     }
   }
+  p.n_tiles = n_tiles_of(p.pair);
+  const int units = units_of(p.pair);
   p.m_tiles = static_cast<int>((M + p.bm - 1) / p.bm);
   const int base_tiles = p.m_tiles * p.n_tiles;
   int s = 1;
@@ -384,7 +398,8 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
     return DQ_ERR_CUDA;
   const uint64_t wrow = fmt == kFmtNF4 ? K / 2 : K;
   if (!make_map_2d(&mw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, wrow, N, wrow,
-                   fmt == kFmtNF4 ? 32 : 64, 128, CU_TENSOR_MAP_SWIZZLE_NONE))
+                   fmt == kFmtNF4 ? 32 : 64, 128,
+                   fmt == kFmtNF4 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B))
     return DQ_ERR_CUDA;
 
   GemmArgs a;

@@ -311,53 +311,56 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
     __syncwarp();
   } else if (warp == C::kMmaWarp) {
     // ------------------------------------------------------------------ MMA
-    if (lane == 0) {
-      int q = 0, acc = 0;
-      uint32_t accphase = 0;
-      uint32_t d_tmem = 0;
-      for (RoundCursor rc = round_begin(args, KB, blockIdx.x, gridDim.x); rc.valid; ++q) {
-        if (rc.kb == rc.tc.kb0) {
-          if (!mbar_wait(accempty_bar(acc), accphase ^ 1u, abort_flag)) break;
-          tc_fence_after();
-          d_tmem = tmem_base + static_cast<uint32_t>(acc * C::kAccStride);
-        }
-        // The dequant warps arrive only after observing the round's X tiles
-        // land, so this one wait covers both operands.
-        DQ_TRACE_POINT(2, q);
-        if (!mbar_wait(afull_bar(q % AR), static_cast<uint32_t>((q / AR) & 1), abort_flag)) break;
-        DQ_TRACE_POINT(3, q);
+    // The whole warp runs the loop (warp-uniform state); one elected lane
+    // issues each tcgen05.mma / commit.  Wait outcomes are agreed warp-wide.
+    int q = 0, acc = 0;
+    uint32_t accphase = 0;
+    uint32_t d_tmem = 0;
+    for (RoundCursor rc = round_begin(args, KB, blockIdx.x, gridDim.x); rc.valid; ++q) {
+      if (rc.kb == rc.tc.kb0) {
+        if (!__all_sync(0xffffffffu, mbar_wait(accempty_bar(acc), accphase ^ 1u, abort_flag))) break;
         tc_fence_after();
+        d_tmem = tmem_base + static_cast<uint32_t>(acc * C::kAccStride);
+      }
+      // The dequant warps arrive only after observing the round's X tiles
+      // land, so this one wait covers both operands.
+      if (lane == 0) DQ_TRACE_POINT(2, q);
+      if (!__all_sync(0xffffffffu,
+                      mbar_wait(afull_bar(q % AR), static_cast<uint32_t>((q / AR) & 1), abort_flag)))
+        break;
+      if (lane == 0) DQ_TRACE_POINT(3, q);
+      tc_fence_after();
 #pragma unroll
-        for (int j = 0; j < R; ++j) {
-          const int kb = rc.kb + j;
-          if (kb < rc.tc.kb1) {
-            const uint64_t bdesc =
-                make_sw128_kmajor_desc(sbase + ((q % XR) * R + j) * C::kXStageBytes);
-            const uint32_t a_tmem =
-                tmem_base + static_cast<uint32_t>(C::kACol0 + ((q % AR) * R + j) * 32);
+      for (int j = 0; j < R; ++j) {
+        const int kb = rc.kb + j;
+        if (kb < rc.tc.kb1) {
+          const uint64_t bdesc = make_sw128_kmajor_desc(sbase + ((q % XR) * R + j) * C::kXStageBytes);
+          const uint32_t a_tmem =
+              tmem_base + static_cast<uint32_t>(C::kACol0 + ((q % AR) * R + j) * 32);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              // K step k: 16 bf16 = 8 TMEM columns of A, 32 bytes along the swizzled B rows.
-              tc_mma_ts(d_tmem, a_tmem + 8u * k, bdesc + static_cast<uint64_t>(2 * k), C::kIdesc,
-                        (kb > rc.tc.kb0 || k > 0) ? 1u : 0u);
-            }
+          for (int k = 0; k < 4; ++k) {
+            // K step k: 16 bf16 = 8 TMEM columns of A, 32 bytes along the swizzled B rows.
+            tc_mma_ts_elect(d_tmem, a_tmem + 8u * k, bdesc + static_cast<uint64_t>(2 * k), C::kIdesc,
+                            (kb > rc.tc.kb0 || k > 0) ? 1u : 0u);
           }
         }
-        tc_commit(done_bar(q % DB));
-        DQ_TRACE_POINT(4, q);
-        const int t_now = rc.t;
-        round_advance<R>(rc, args, KB);
-        if (!rc.valid || rc.t != t_now) {
-          tc_commit(accfull_bar(acc));
-          if (++acc == C::kNumAcc) { acc = 0; accphase ^= 1u; }
-        }
       }
-      if (*abort_flag) {
-        // Wait (bounded) until every MMA this thread issued has retired.
-        tc_commit(drain_bar);
-        volatile int never = 0;
-        mbar_wait(drain_bar, 0, &never, 100000000ull);
+      tc_commit_elect(done_bar(q % DB));
+      if (lane == 0) DQ_TRACE_POINT(4, q);
+      const int t_now = rc.t;
+      round_advance<R>(rc, args, KB);
+      if (!rc.valid || rc.t != t_now) {
+        tc_commit_elect(accfull_bar(acc));
+        if (++acc == C::kNumAcc) { acc = 0; accphase ^= 1u; }
       }
+      __syncwarp();
+    }
+    if (*abort_flag) {
+      // Wait (bounded) until every MMA this warp issued has retired.
+      __syncwarp();
+      tc_commit_elect(drain_bar);
+      volatile int never = 0;
+      mbar_wait(drain_bar, 0, &never, 100000000ull);
     }
     __syncwarp();
   } else if (warp >= 4) {
@@ -366,6 +369,11 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
     const int quad = warp & 3;           // TMEM lane quadrant this warp may access
     const int group = dw >> 2;           // this warp decodes k-blocks j = group, group + G, ...
     const int r = quad * 32 + lane;      // weight row within the tile
+    // The weight tile lands with the TMA 32-byte (NF4) / 64-byte (fp8)
+    // swizzle: 16-byte chunk c of row r sits at chunk c ^ (r>>2 & 1) /
+    // c ^ (r>>1 & 3), so the eight lanes of each 128-bit load phase hit
+    // distinct banks.
+    const uint32_t wsw = FMT == kFmtNF4 ? ((r >> 2) & 1) : ((r >> 1) & 3);
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     float sfp8 = 0.f;
     if constexpr (FMT == kFmtFP8) sfp8 = __bfloat162float(__float2bfloat16_rn(args.fp8_scale));
@@ -405,7 +413,7 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
           const uint32_t wrow = sbase + C::kOffW + ws * C::kWStageBytes + r * C::kWBytes;
           uint4 pk[C::kWBytes / 16];
 #pragma unroll
-          for (int i = 0; i < C::kWBytes / 16; ++i) pk[i] = lds128(wrow + 16u * i);
+          for (int i = 0; i < C::kWBytes / 16; ++i) pk[i] = lds128(wrow + 16u * (i ^ wsw));
           // the producer's next TMA into this stage must not overtake these reads
           fence_proxy_async_smem();
           __syncwarp();

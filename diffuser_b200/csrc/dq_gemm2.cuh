@@ -40,7 +40,10 @@ struct Gemm2Cfg {
   static constexpr int kNumAcc = BM <= 192 ? 2 : 1;
   static constexpr int kAccStride = BM;
   static constexpr int kACol0 = ((kNumAcc * kAccStride + 31) / 32) * 32;
-  static constexpr int kRound = BM >= 256 ? 1 : (BM >= 128 ? 2 : 4);
+  // k-blocks per MMA round.  Two k-blocks even at BM=256 (1024 cycles of
+  // tensor work per round): one k-block per round leaves the tensor core idle
+  // during the MMA warp's per-round wait + commit handshake.
+  static constexpr int kRound = BM >= 128 ? 2 : 4;
   static constexpr int kDqGroups = 2;
   static constexpr int kDqWarps = 4 * kDqGroups;
   static constexpr int kWProducerWarp = 4 + kDqWarps;
@@ -213,20 +216,23 @@ __global__ void __launch_bounds__(Gemm2Cfg<FMT, BM>::kThreads, 1)
     __syncwarp();
   } else if (warp == C::kMmaWarp) {
     // ------------------------------------------------------- MMA (leader)
-    if (leader && lane == 0) {
+    // Whole-warp loop, one elected lane issues (see the one-CTA kernel).
+    if (leader) {
       int q = 0, acc = 0;
       uint32_t accphase = 0;
       uint32_t d_tmem = 0;
       for (RoundCursor rc = round_begin(args, KB, pair, npairs); rc.valid; ++q) {
         if (rc.kb == rc.tc.kb0) {
-          if (!mbar_wait_cluster(accempty_bar(acc), accphase ^ 1u, abort_flag)) break;
+          if (!__all_sync(0xffffffffu, mbar_wait_cluster(accempty_bar(acc), accphase ^ 1u, abort_flag)))
+            break;
           tc_fence_after();
           d_tmem = tmem_base + static_cast<uint32_t>(acc * C::kAccStride);
         }
-        DQ_TRACE_POINT(2, q);
-        if (!mbar_wait_cluster(afull_bar(q % AR), static_cast<uint32_t>((q / AR) & 1), abort_flag))
+        if (lane == 0) DQ_TRACE_POINT(2, q);
+        if (!__all_sync(0xffffffffu, mbar_wait_cluster(afull_bar(q % AR),
+                                                       static_cast<uint32_t>((q / AR) & 1), abort_flag)))
           break;
-        DQ_TRACE_POINT(3, q);
+        if (lane == 0) DQ_TRACE_POINT(3, q);
         tc_fence_after();
 #pragma unroll
         for (int j = 0; j < R; ++j) {
@@ -238,21 +244,23 @@ __global__ void __launch_bounds__(Gemm2Cfg<FMT, BM>::kThreads, 1)
                 tmem_base + static_cast<uint32_t>(C::kACol0 + ((q % AR) * R + j) * 32);
 #pragma unroll
             for (int k = 0; k < 4; ++k)
-              tc_mma_ts_pair(d_tmem, a_tmem + 8u * k, bdesc + static_cast<uint64_t>(2 * k), C::kIdesc,
-                             (kb > rc.tc.kb0 || k > 0) ? 1u : 0u);
+              tc_mma_ts_pair_elect(d_tmem, a_tmem + 8u * k, bdesc + static_cast<uint64_t>(2 * k),
+                                   C::kIdesc, (kb > rc.tc.kb0 || k > 0) ? 1u : 0u);
           }
         }
-        tc_commit_pair(done_bar(q % DB));
-        DQ_TRACE_POINT(4, q);
+        tc_commit_pair_elect(done_bar(q % DB));
+        if (lane == 0) DQ_TRACE_POINT(4, q);
         const int t_now = rc.t;
         round_advance<R>(rc, args, KB);
         if (!rc.valid || rc.t != t_now) {
-          tc_commit_pair(accfull_bar(acc));
+          tc_commit_pair_elect(accfull_bar(acc));
           if (++acc == C::kNumAcc) { acc = 0; accphase ^= 1u; }
         }
+        __syncwarp();
       }
       if (*abort_flag) {
-        tc_commit_pair(drain_bar);
+        __syncwarp();
+        tc_commit_pair_elect(drain_bar);
         volatile int never = 0;
         mbar_wait(drain_bar, 0, &never, 100000000ull);
       }
@@ -264,6 +272,11 @@ __global__ void __launch_bounds__(Gemm2Cfg<FMT, BM>::kThreads, 1)
     const int quad = warp & 3;
     const int group = dw >> 2;
     const int r = quad * 32 + lane;      // weight row within this CTA's 128
+    // The weight tile lands with the TMA 32-byte (NF4) / 64-byte (fp8)
+    // swizzle: 16-byte chunk c of row r sits at chunk c ^ (r>>2 & 1) /
+    // c ^ (r>>1 & 3), so the eight lanes of each 128-bit load phase hit
+    // distinct banks.
+    const uint32_t wsw = FMT == kFmtNF4 ? ((r >> 2) & 1) : ((r >> 1) & 3);
     const int r_tile = static_cast<int>(rank) * 128 + r;  // row within the pair's 256
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     float sfp8 = 0.f;
@@ -303,7 +316,7 @@ __global__ void __launch_bounds__(Gemm2Cfg<FMT, BM>::kThreads, 1)
           const uint32_t wrow = sbase + C::kOffW + ws * C::kWStageBytes + r * C::kWBytes;
           uint4 pk[C::kWBytes / 16];
 #pragma unroll
-          for (int i = 0; i < C::kWBytes / 16; ++i) pk[i] = lds128(wrow + 16u * i);
+          for (int i = 0; i < C::kWBytes / 16; ++i) pk[i] = lds128(wrow + 16u * (i ^ wsw));
           // the producer's next TMA into this stage must not overtake these reads
           fence_proxy_async_smem();
           __syncwarp();
