@@ -33,6 +33,7 @@ SIGNATURES = {
     "dq_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), _c_p]),
     "dq_set_tile_override": (ctypes.c_int, [ctypes.c_int, ctypes.c_int]),
     "dq_set_pair_mode": (ctypes.c_int, [ctypes.c_int]),
+    "dq_plan_info": (ctypes.c_int, [_c_i64, _c_i64, _c_i64, ctypes.c_int] + [ctypes.POINTER(ctypes.c_int)] * 4),
 }
 
 DQ_OK = 0

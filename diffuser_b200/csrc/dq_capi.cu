@@ -543,6 +543,23 @@ size_t dq_workspace_size(int64_t M, int64_t N, int64_t K, int fmt) {
   return make_plan(M, N, K, d->sms).ws;
 }
 
+int dq_plan_info(int64_t M, int64_t N, int64_t K, int fmt, int* pair, int* bm, int* splits,
+                 int* grid) {
+  if (pair == nullptr || bm == nullptr || splits == nullptr || grid == nullptr) return DQ_ERR_ARG;
+  if (M <= 0 || N <= 0 || K <= 0 || (fmt != DQ_FMT_NF4 && fmt != DQ_FMT_FP8) ||
+      (K % (fmt == DQ_FMT_NF4 ? 64 : 16)) != 0)
+    return DQ_ERR_SHAPE;
+  DeviceInfo* d = nullptr;
+  const int rc = current_device(&d);
+  if (rc != DQ_OK) return rc;
+  const Plan p = make_plan(M, N, K, d->sms);
+  *pair = p.pair ? 1 : 0;
+  *bm = p.bm;
+  *splits = p.splits;
+  *grid = p.pair ? 2 * p.grid : p.grid;
+  return DQ_OK;
+}
+
 int dq_linear_nf4(const void* x, int64_t M, int64_t K, const uint8_t* packed, const float* absmax,
                   const void* bias, int64_t N, void* y, void* workspace, size_t workspace_bytes,
                   dq_stream_t stream) {

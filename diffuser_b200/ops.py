@@ -226,3 +226,13 @@ def set_pair_mode(mode: int = 0) -> None:
 def set_tile_override(bm: int = 0, splits: int = 0) -> None:
     """Force the x-tile height / split-K count (0 = automatic); for sweeps."""
     _lib.check("dq_set_tile_override", _lib.lib().dq_set_tile_override(int(bm), int(splits)))
+
+
+def plan_info(M: int, N: int, K: int, fmt: int = _lib.DQ_FMT_NF4) -> dict:
+    """The launch plan the linear uses for this shape on the current device."""
+    vals = [ctypes.c_int(0) for _ in range(4)]
+    _lib.check("dq_plan_info", _lib.lib().dq_plan_info(int(M), int(N), int(K), int(fmt),
+                                                       *[ctypes.byref(v) for v in vals]))
+    pair, bm, splits, grid = (v.value for v in vals)
+    return {"kernel": "dq_gemm2_kernel (CTA pair)" if pair else "dq_gemm_kernel (one CTA)",
+            "pair": bool(pair), "bm": bm, "splits": splits, "grid": grid}

@@ -133,6 +133,13 @@ int dq_set_tile_override(int bm, int splits);
  * tile (128 weight rows), 2 = CTA-pair tiles (256 weight rows, x-tile >= 64). */
 int dq_set_pair_mode(int mode);
 
+/* Describes the launch plan dq_linear_* uses for this shape on the current
+ * device: *pair = 1 for CTA-pair tiles (256 weight rows per tile) or 0 for
+ * one-CTA tiles (128 rows), *bm = x-tile rows, *splits = split-K count,
+ * *grid = CTAs launched.  A diagnostic query with no reference counterpart. */
+int dq_plan_info(int64_t M, int64_t N, int64_t K, int fmt, int* pair, int* bm, int* splits,
+                 int* grid);
+
 #ifdef __cplusplus
 }
 #endif

@@ -86,3 +86,12 @@ def test_product_path_refuses_cpu_tensors():
                        torch.zeros(64 * 8 // 2, dtype=torch.uint8), torch.ones(8), 8)
     with pytest.raises(RuntimeError, match="CUDA"):
         ops.ltx23_nf4_quantize(torch.zeros(64))
+
+
+def test_plan_info_rejects_bad_arguments_on_host(lib):
+    v = [ctypes.c_int(0) for _ in range(4)]
+    refs = [ctypes.byref(x) for x in v]
+    assert lib.dq_plan_info(4, 8, 100, 0, *refs) == 1      # NF4 needs K % 64 == 0
+    assert lib.dq_plan_info(0, 8, 64, 0, *refs) == 1       # empty batch has no plan
+    assert lib.dq_plan_info(4, 8, 64, 5, *refs) == 1       # unknown format
+    assert lib.dq_plan_info(4, 8, 64, 0, None, *refs[1:]) == 7

@@ -199,5 +199,13 @@ def test_golden_linear(ops):
     assert R.rel_err(to_bits(y2), g["fp8_y"]) <= TOL
 
 
+def test_plan_choice(ops):
+    # large token batches take CTA-pair tiles, decode-sized batches one-CTA tiles
+    big = ops.plan_info(4608, 12288, 3072)
+    assert big["pair"] and big["bm"] == 256 and big["splits"] == 1
+    small = ops.plan_info(16, 3072, 3072)
+    assert not small["pair"] and small["bm"] == 16 and small["splits"] > 1
+
+
 def test_no_kernel_error_recorded(ops):
     assert ops.device_error() == 0
