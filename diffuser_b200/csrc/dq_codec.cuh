@@ -115,17 +115,23 @@ __device__ __forceinline__ void nf4_decode_word(uint32_t w, const Nf4Planes& P, 
 // banks.  32 KB.
 constexpr int kNf4LutBytes = 256 * 32 * 4;
 
+// The 16 level patterns in constant memory: the LUT fill reads them with a
+// warp-uniform index (a broadcast), where a per-thread copy of the table would
+// be indexed dynamically and live in local memory.
+__constant__ uint16_t c_nf4_level_bits[16] = {
+    kNf4LevelBits[0],  kNf4LevelBits[1],  kNf4LevelBits[2],  kNf4LevelBits[3],
+    kNf4LevelBits[4],  kNf4LevelBits[5],  kNf4LevelBits[6],  kNf4LevelBits[7],
+    kNf4LevelBits[8],  kNf4LevelBits[9],  kNf4LevelBits[10], kNf4LevelBits[11],
+    kNf4LevelBits[12], kNf4LevelBits[13], kNf4LevelBits[14], kNf4LevelBits[15]};
+
 // Fill the LUT (called by every thread of the CTA; caller synchronizes).
+// Entry b of lane l is word b * 32 + l: each warp writes one byte value b for
+// all 32 lanes per iteration (blockDim.x is a multiple of 32).
 __device__ __forceinline__ void nf4_lut_fill(uint32_t* lut) {
   for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) {
     const int b = i >> 5;
-    constexpr uint16_t t[16] = {kNf4LevelBits[0],  kNf4LevelBits[1],  kNf4LevelBits[2],
-                                kNf4LevelBits[3],  kNf4LevelBits[4],  kNf4LevelBits[5],
-                                kNf4LevelBits[6],  kNf4LevelBits[7],  kNf4LevelBits[8],
-                                kNf4LevelBits[9],  kNf4LevelBits[10], kNf4LevelBits[11],
-                                kNf4LevelBits[12], kNf4LevelBits[13], kNf4LevelBits[14],
-                                kNf4LevelBits[15]};
-    lut[i] = static_cast<uint32_t>(t[b >> 4]) | (static_cast<uint32_t>(t[b & 15]) << 16);
+    lut[i] = static_cast<uint32_t>(c_nf4_level_bits[b >> 4]) |
+             (static_cast<uint32_t>(c_nf4_level_bits[b & 15]) << 16);
   }
 }
 

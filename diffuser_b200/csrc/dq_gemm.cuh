@@ -13,11 +13,12 @@
 //     warps that add the bias, round to bf16 and store Y row-major.
 // Warp roles (one persistent CTA per SM, static round-robin over tiles):
 //   warps 0-3     epilogue (warp w owns TMEM lanes 32w..32w+31)
-//   warps 4-11    dequant, two groups of four; a group decodes every other
-//                 k-block of a round (warp w writes TMEM lanes 32(w%4)..)
-//   warp 12       weight producer (TMA of the packed weight, deep ring)
-//   warp 13       MMA issuer (one thread) and TMEM allocator
-//   warp 14       activation producer (TMA of X tiles)
+//   warps 4..     dequant, G groups of four (G = 2, or 4 for BM <= 64); the
+//                 groups take turns by k-block (warp w writes TMEM lanes
+//                 32(w%4)..)
+//   then          weight producer (TMA of the packed weight, deep ring),
+//                 MMA warp (elected lane issues; TMEM allocator),
+//                 activation producer (TMA of X tiles)
 // Three rings decouple the operands' lifetimes: packed-weight stages are
 // released as soon as the dequant warps have read them, so the weight ring
 // runs far ahead; X stages and TMEM A stages are released per ROUND by one
@@ -80,9 +81,12 @@ struct GemmCfg {
   static constexpr int kNumAcc = BM <= 192 ? 2 : 1;             // accumulator buffers
   static constexpr int kAccStride = BM < 32 ? 32 : BM;          // TMEM columns per accumulator
   static constexpr int kACol0 = ((kNumAcc * kAccStride + 31) / 32) * 32;
-  // k-blocks per MMA round: enough tensor work per handshake (>= ~512 cycles).
-  static constexpr int kRound = BM >= 256 ? 1 : (BM >= 128 ? 2 : 4);
-  static constexpr int kDqGroups = 2;
+  // k-blocks per MMA round (the measured best: 2, and 1 for BM=256).
+  static constexpr int kRound = BM >= 256 ? 1 : 2;
+  // Small tiles carry little MMA work per k-block, so the decode rate sets the
+  // pace: four groups of dequant warps (and deeper rings) for BM <= 64.
+  static constexpr bool kSmall = BM <= 64;
+  static constexpr int kDqGroups = kSmall ? 4 : 2;
   static constexpr int kDqWarps = 4 * kDqGroups;
   static constexpr int kWProducerWarp = 4 + kDqWarps;
   static constexpr int kMmaWarp = 5 + kDqWarps;
@@ -95,17 +99,20 @@ struct GemmCfg {
   static constexpr int kSmemLimit = 227 * 1024;
   // NF4 decodes through a 32 KB shared byte LUT (dq_codec.cuh)
   static constexpr int kLutBytes = FMT == kFmtNF4 ? kNf4LutBytes : 0;
-  // weight ring: 32 KB (NF4) / 48 KB (fp8) of packed tiles
-  static constexpr int kWStages = ((FMT == kFmtNF4 ? 32 : 48) * 1024) / kWStageBytes;
+  // weight ring: 32 KB (NF4) / 48 KB (fp8) of packed tiles, 96 / 128 KB for small tiles
+  static constexpr int kWStages =
+      ((kSmall ? (FMT == kFmtNF4 ? 96 : 128) : (FMT == kFmtNF4 ? 32 : 48)) * 1024) / kWStageBytes;
   // activation ring: rounds of X tiles in the rest
   static constexpr int kXRoundsFit =
       (kSmemLimit - kEpiBytes - 2048 - kLutBytes - kWStages * kWStageBytes) / (kRound * kXStageBytes);
-  static constexpr int kXRounds = kXRoundsFit > 4 ? 4 : kXRoundsFit;
+  static constexpr int kXRoundsMax = kSmall ? 8 : 4;
+  static constexpr int kXRounds = kXRoundsFit > kXRoundsMax ? kXRoundsMax : kXRoundsFit;
   static_assert(kXRounds >= 2, "need two rounds of X tiles in flight");
   static constexpr int kXStages = kXRounds * kRound;
   // TMEM A ring
   static constexpr int kARoundsFit = (512 - kACol0) / 32 / kRound;
-  static constexpr int kARounds = kARoundsFit > 4 ? 4 : kARoundsFit;
+  static constexpr int kARoundsMax = kSmall ? 8 : 4;
+  static constexpr int kARounds = kARoundsFit > kARoundsMax ? kARoundsMax : kARoundsFit;
   static_assert(kARounds >= 2, "need two rounds of TMEM A stages");
   static constexpr int kAStages = kARounds * kRound;
   // one completion barrier per round, shared by the X and A rings
