@@ -53,7 +53,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="nf4")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["tp_fp8"], default="nf4")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
@@ -165,6 +165,16 @@ def max_over_ranks(val: float, world: int, device) -> float:
     t = torch.tensor([val], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def gather_ranks(val: float, world: int, device) -> list:
+    if world == 1:
+        return [val]
+    import torch.distributed as dist
+    t = torch.tensor([val], dtype=torch.float64, device=device)
+    out = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(o.item()) for o in out]
 
 
 def barrier(world: int):
@@ -315,6 +325,7 @@ def run_ours(args, world, rank, local):
     kern_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
     el_ms_max = max_over_ranks(el_ms, world, dev)
     kern_ms_max = max_over_ranks(kern_ms, world, dev)
+    kern_ms_ranks = gather_ranks(kern_ms, world, dev)
     err = ops.device_error(dev)
     if err != 0:
         raise RuntimeError(f"kernel error word {err}")
@@ -407,6 +418,7 @@ def run_ours(args, world, rank, local):
                          "frac": achieved / peak_tf, "traffic": traffic,
                          "peak_source": f"{peak_src} bf16 dense (burst)",
                          "kernel": f"{plan['kernel']} {fmt} BM={plan['bm']}", "kernel_ms": kern_ms_max,
+                         "kernel_ms_per_rank": kern_ms_ranks,
                          "algorithmic_bytes": WORKLOADS[fmt]["bytes"]},
             "cpu_baseline": cpu,
             "e2e": e2e,
@@ -419,11 +431,93 @@ def run_ours(args, world, rank, local):
         dist.destroy_process_group()
 
 
+# ------------------------------------------------------- column-parallel
+TP_M, TP_N, TP_K = 6144, 12288, 4096  # LTX video tokens x fused q/k/v projection (4096 -> 3 x 4096)
+
+
+def run_tp(args, world, rank, local):
+    """Column-parallel fp8 linear x[6144,4096] . W[12288,4096]^T over `world`
+    GPUs: total work fixed (strong scaling).  Each rank's fused kernel writes
+    its [M, N/world] block into every rank's y through NVLink peer stores."""
+    import torch.distributed as dist
+    from diffuser_b200 import ops, tp
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    else:
+        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:29599", rank=0, world_size=1)
+    g0 = torch.Generator(device=dev).manual_seed(0)
+    w = torch.randn(TP_N, TP_K, generator=g0, device=dev) * 0.02
+    w8, s0 = ops.fp8_quantize(w)
+    del w
+    grp = tp.TpGroup(TP_M, TP_N)
+    mod = tp.ColumnParallelFp8Linear(TP_K, TP_N, grp, bias=False).to(dev)
+    mod.set_fp8_weight(w8, float(s0.item()))
+    del w8
+    xs = [torch.randn(TP_M, TP_K, generator=torch.Generator(device=dev).manual_seed(1 + i),
+                      device=dev).to(torch.bfloat16) for i in range(2)]
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn, steps):
+        for i in range(max(args.warmup, 3)):
+            fn(i)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world)
+        torch.cuda.synchronize()
+        a.record(stream)
+        for i in range(steps):
+            fn(i)
+        b.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        return max_over_ranks(a.elapsed_time(b) / steps, world, dev)
+
+    with ClockSampler(local) as clk:
+        fused_ms = timed(lambda i: mod(xs[i % 2]), args.steps)
+    err = ops.device_error(dev)
+    nccl_ms = None
+    if world > 1:
+        nccl_ms = timed(lambda i: mod.forward_nccl(xs[i % 2]), max(10, args.steps // 4))
+    grp.close()
+    flops = 2 * TP_M * TP_N * TP_K
+    peer_bytes = (world - 1) * TP_M * (TP_N // world) * 2  # sent by each rank
+    if rank == 0:
+        peak_tf, _, peak_src = measured_peaks()
+        line = {
+            "metric": "column-parallel fp8 linear TFLOP/s", "value": flops / (fused_ms * 1e-3) / 1e12,
+            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": fused_ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"fp8_linear x[{TP_M},{TP_K}]bf16 . W[{TP_N},{TP_K}]e4m3^T split over "
+                                   f"{world} GPUs by out_features", "parallelism": f"tp{world} column-parallel",
+                       "collective": "fused: epilogue peer stores + flag barrier"},
+            "per_gpu_tflops": flops / world / (fused_ms * 1e-3) / 1e12,
+            "nvlink_gbs_per_gpu": peer_bytes / (fused_ms * 1e-3) / 1e9,
+            "compute_bound_ms": flops / world / (peak_tf * 1e12) * 1e3,
+            "nccl_allgather_path_ms": nccl_ms,
+            "peak_source": f"{peak_src} bf16 dense (burst)",
+            "device_error": err, "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    dist.destroy_process_group()
+
+
 def main():
     args = parse()
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
+        if args.workload == "tp_fp8":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable":
+                                  "the reference runs each linear on one GPU; it has no column-parallel path"}))
+            return
         run_reference_arm(args, world, rank)
+        return
+    if args.workload == "tp_fp8":
+        run_tp(args, world, rank, local)
         return
     run_ours(args, world, rank, local)
 

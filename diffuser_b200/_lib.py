@@ -33,6 +33,19 @@ SIGNATURES = {
     "dq_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), _c_p]),
     "dq_set_tile_override": (ctypes.c_int, [ctypes.c_int, ctypes.c_int]),
     "dq_set_pair_mode": (ctypes.c_int, [ctypes.c_int]),
+    "dq_tp_buffer_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
+    "dq_tp_buffer_free": (ctypes.c_int, [ctypes.c_void_p]),
+    "dq_ipc_handle": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "dq_ipc_open": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "dq_ipc_close": (ctypes.c_int, [ctypes.c_void_p]),
+    "dq_tp_linear_nf4": (ctypes.c_int, [ctypes.c_void_p, _c_i64, _c_i64, ctypes.c_void_p, ctypes.c_void_p,
+                                        ctypes.c_void_p, _c_i64, ctypes.c_int, ctypes.c_int,
+                                        ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p),
+                                        ctypes.c_void_p, ctypes.c_uint, ctypes.c_void_p]),
+    "dq_tp_linear_fp8": (ctypes.c_int, [ctypes.c_void_p, _c_i64, _c_i64, ctypes.c_void_p, ctypes.c_float,
+                                        ctypes.c_void_p, _c_i64, ctypes.c_int, ctypes.c_int,
+                                        ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p),
+                                        ctypes.c_void_p, ctypes.c_uint, ctypes.c_void_p]),
     "dq_plan_info": (ctypes.c_int, [_c_i64, _c_i64, _c_i64, ctypes.c_int] + [ctypes.POINTER(ctypes.c_int)] * 4),
 }
 
@@ -40,6 +53,7 @@ DQ_OK = 0
 DQ_ERR_TIMEOUT = 5
 DQ_ERR_SCRATCH_LIMIT = 9
 DQ_NOALLOC_SCRATCH_BYTES = 8 << 20
+DQ_IPC_HANDLE_BYTES = 64
 DQ_FMT_NF4, DQ_FMT_FP8 = 0, 1
 DQ_DTYPE_F32, DQ_DTYPE_BF16 = 0, 1
 

@@ -9,6 +9,7 @@
 #include <atomic>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "../../include/dq_linear.h"
@@ -126,6 +127,26 @@ __global__ void finalize_fp8_scale_kernel(unsigned int* amax_bits_then_scale) {
   *reinterpret_cast<float*>(amax_bits_then_scale) = s;
 }
 
+// Column-parallel completion: thread r waits (bounded) until rank r has raised
+// its flag in this rank's flag array to `epoch`; on expiry the device error
+// word records DQ_ERR_TIMEOUT and the wait ends.
+__global__ void tp_wait_kernel(const unsigned int* flags, int world, unsigned int epoch,
+                               unsigned long long limit_ns) {
+  const int r = threadIdx.x;
+  if (r >= world) return;
+  const unsigned long long t0 = globaltimer_ns();
+  while (true) {
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + r) : "memory");
+    if (static_cast<int>(v - epoch) >= 0) return;
+    if (globaltimer_ns() - t0 > limit_ns) {
+      atomicOr(&g_dq_error, 1u << kErrTimeout);
+      return;
+    }
+    __nanosleep(256);
+  }
+}
+
 // Split-K: y = bf16(sum_s partial[s] + bias); four outputs per thread.
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int M, int N,
                                      const __nv_bfloat16* __restrict__ bias,
@@ -144,9 +165,9 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits,
 struct DeviceInfo {
   int ok = 0;  // 1 = probed
   int major = 0, minor = 0, sms = 0;
-  int smem_set[2][6] = {};
-  int smem_set2[2][6] = {};
-  int max_pairs[2][6] = {};
+  int smem_set[2][2][6] = {};   // [column-parallel][fmt][bm]
+  int smem_set2[2][2][6] = {};
+  int max_pairs[2][6] = {};     // [fmt][bm]
 };
 
 constexpr int kMaxDevices = 64;
@@ -232,7 +253,7 @@ struct TileShape {
 static constexpr TileShape kShapes[] = {
     {false, 128, 0.72}, {false, 192, 1.0}, {false, 256, 0.97}, {true, 192, 0.93}, {true, 256, 1.13}};
 
-static Plan make_plan(int64_t M, int64_t N, int64_t K, int sms) {
+static Plan make_plan(int64_t M, int64_t N, int64_t K, int sms, bool allow_split = true) {
   Plan p;
   const int KB = static_cast<int>((K + 63) / 64);
   const int opair = g_override_pair.load();  // 0 automatic, 1 one-CTA only, 2 pairs only
@@ -278,10 +299,10 @@ static Plan make_plan(int64_t M, int64_t N, int64_t K, int sms) {
   const int os = g_override_splits.load();
   if (os > 0) {
     s = os;
-  } else if (base_tiles * 2 <= units && KB >= 8) {
+  } else if (allow_split && base_tiles * 2 <= units && KB >= 8) {
     s = std::min(std::min(units / base_tiles, KB / 4), 16);
   }
-  s = std::max(1, std::min(s, KB));
+  s = allow_split ? std::max(1, std::min(s, KB)) : 1;
   p.kb_per_split = (KB + s - 1) / s;
   p.splits = (KB + p.kb_per_split - 1) / p.kb_per_split;
   p.tiles = base_tiles * p.splits;
@@ -290,30 +311,47 @@ static Plan make_plan(int64_t M, int64_t N, int64_t K, int sms) {
   return p;
 }
 
-template <int FMT, int BM>
+template <int FMT, int BM, bool TP>
 static int launch_gemm(DeviceInfo* d, const Plan& p, const CUtensorMap& mx, const CUtensorMap& mw,
                        const GemmArgs& a, cudaStream_t st) {
   using C = GemmCfg<FMT, BM>;
-  auto kern = dq_gemm_kernel<FMT, BM>;
+  auto kern = dq_gemm_kernel<FMT, BM, TP>;
   const int bi = bm_index(BM);
-  if (!d->smem_set[FMT][bi]) {
+  if (!d->smem_set[TP][FMT][bi]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
         cudaSuccess)
       return DQ_ERR_LAUNCH;
-    d->smem_set[FMT][bi] = 1;
+    d->smem_set[TP][FMT][bi] = 1;
   }
   kern<<<p.grid, C::kThreads, C::kSmemBytes, st>>>(mx, mw, a);
   return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
 }
 
-template <int FMT, int BM>
-static int launch_gemm2(DeviceInfo* d, const Plan& p, const CUtensorMap& mx, const CUtensorMap& mw,
-                        const GemmArgs& a, cudaStream_t st) {
+// One-time setup of a pair-kernel instantiation on this device: shared-memory
+// opt-in and the number of two-CTA clusters that can be resident at once
+// (cached in d->max_pairs; the persistent grid never exceeds it).
+template <int FMT, int BM, bool TP>
+static int pair_setup(DeviceInfo* d, cudaLaunchConfig_t& cfg) {
   using C = Gemm2Cfg<FMT, BM>;
-  auto kern = dq_gemm2_kernel<FMT, BM>;
+  auto kern = dq_gemm2_kernel<FMT, BM, TP>;
   const int bi = bm_index(BM);
+  if (d->smem_set2[TP][FMT][bi]) return DQ_OK;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
+      cudaSuccess)
+    return DQ_ERR_LAUNCH;
+  int clusters = 0;
+  cfg.gridDim = dim3(2 * std::max(1, d->sms / 2));
+  if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1)
+    return DQ_ERR_LAUNCH;
+  d->max_pairs[FMT][bi] = clusters;
+  d->smem_set2[TP][FMT][bi] = 1;
+  return DQ_OK;
+}
+
+template <int FMT, int BM>
+static cudaLaunchConfig_t pair_config(cudaLaunchAttribute* attr, cudaStream_t st) {
+  using C = Gemm2Cfg<FMT, BM>;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
@@ -323,42 +361,57 @@ static int launch_gemm2(DeviceInfo* d, const Plan& p, const CUtensorMap& mx, con
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (!d->smem_set2[FMT][bi]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
-        cudaSuccess)
-      return DQ_ERR_LAUNCH;
-    int clusters = 0;
-    cfg.gridDim = dim3(2 * std::max(1, d->sms / 2));
-    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1)
-      return DQ_ERR_LAUNCH;
-    d->max_pairs[FMT][bi] = clusters;
-    d->smem_set2[FMT][bi] = 1;
-  }
-  const int pairs = std::max(1, std::min(p.grid, d->max_pairs[FMT][bi]));
+  return cfg;
+}
+
+template <int FMT, int BM, bool TP>
+static int launch_gemm2(DeviceInfo* d, const Plan& p, const CUtensorMap& mx, const CUtensorMap& mw,
+                        const GemmArgs& a, cudaStream_t st) {
+  auto kern = dq_gemm2_kernel<FMT, BM, TP>;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = pair_config<FMT, BM>(attr, st);
+  const int rc = pair_setup<FMT, BM, TP>(d, cfg);
+  if (rc != DQ_OK) return rc;
+  const int pairs = std::max(1, std::min(p.grid, d->max_pairs[FMT][bm_index(BM)]));
   cfg.gridDim = dim3(2 * pairs);
   if (cudaLaunchKernelEx(&cfg, kern, mx, mw, a) != cudaSuccess) return DQ_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
 }
 
+// Resident-cluster capacity of the pair kernel for (FMT, bm) on this device.
 template <int FMT>
+static int pair_capacity(DeviceInfo* d, int bm, int* pairs) {
+  cudaLaunchAttribute attr[1];
+  int rc = DQ_ERR_ARG;
+  switch (bm) {
+    case 64: { auto c = pair_config<FMT, 64>(attr, nullptr); rc = pair_setup<FMT, 64, false>(d, c); break; }
+    case 128: { auto c = pair_config<FMT, 128>(attr, nullptr); rc = pair_setup<FMT, 128, false>(d, c); break; }
+    case 192: { auto c = pair_config<FMT, 192>(attr, nullptr); rc = pair_setup<FMT, 192, false>(d, c); break; }
+    case 256: { auto c = pair_config<FMT, 256>(attr, nullptr); rc = pair_setup<FMT, 256, false>(d, c); break; }
+  }
+  if (rc == DQ_OK) *pairs = d->max_pairs[FMT][bm_index(bm)];
+  return rc;
+}
+
+template <int FMT, bool TP>
 static int dispatch_gemm(DeviceInfo* d, const Plan& p, const CUtensorMap& mx, const CUtensorMap& mw,
                          const GemmArgs& a, cudaStream_t st) {
   if (p.pair) {
     switch (p.bm) {
-      case 64: return launch_gemm2<FMT, 64>(d, p, mx, mw, a, st);
-      case 128: return launch_gemm2<FMT, 128>(d, p, mx, mw, a, st);
-      case 192: return launch_gemm2<FMT, 192>(d, p, mx, mw, a, st);
-      case 256: return launch_gemm2<FMT, 256>(d, p, mx, mw, a, st);
+      case 64: return launch_gemm2<FMT, 64, TP>(d, p, mx, mw, a, st);
+      case 128: return launch_gemm2<FMT, 128, TP>(d, p, mx, mw, a, st);
+      case 192: return launch_gemm2<FMT, 192, TP>(d, p, mx, mw, a, st);
+      case 256: return launch_gemm2<FMT, 256, TP>(d, p, mx, mw, a, st);
     }
     return DQ_ERR_ARG;
   }
   switch (p.bm) {
-    case 16: return launch_gemm<FMT, 16>(d, p, mx, mw, a, st);
-    case 32: return launch_gemm<FMT, 32>(d, p, mx, mw, a, st);
-    case 64: return launch_gemm<FMT, 64>(d, p, mx, mw, a, st);
-    case 128: return launch_gemm<FMT, 128>(d, p, mx, mw, a, st);
-    case 192: return launch_gemm<FMT, 192>(d, p, mx, mw, a, st);
-    case 256: return launch_gemm<FMT, 256>(d, p, mx, mw, a, st);
+    case 16: return launch_gemm<FMT, 16, TP>(d, p, mx, mw, a, st);
+    case 32: return launch_gemm<FMT, 32, TP>(d, p, mx, mw, a, st);
+    case 64: return launch_gemm<FMT, 64, TP>(d, p, mx, mw, a, st);
+    case 128: return launch_gemm<FMT, 128, TP>(d, p, mx, mw, a, st);
+    case 192: return launch_gemm<FMT, 192, TP>(d, p, mx, mw, a, st);
+    case 256: return launch_gemm<FMT, 256, TP>(d, p, mx, mw, a, st);
   }
   return DQ_ERR_ARG;
 }
@@ -373,9 +426,21 @@ static int grid_for(int64_t work, int threads, int sms) {
   return static_cast<int>(std::max<int64_t>(g, 1));
 }
 
+// Column-parallel call: this rank's N columns go to column rank * N of every
+// rank's y [M, N * world].
+struct TpOpts {
+  int rank, world;
+  void* const* y_ranks;
+  unsigned int* const* flag_ranks;
+  unsigned int* counter;
+  unsigned int epoch;
+};
+
+static constexpr unsigned long long kTpWaitNs = 5000000000ull;  // 5 s
+
 static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8_t* w,
                        const float* absmax, float scale, const void* bias, int64_t N, void* y,
-                       void* ws, size_t ws_bytes, cudaStream_t st) {
+                       void* ws, size_t ws_bytes, cudaStream_t st, const TpOpts* tp = nullptr) {
   // NF4 blocks of 64 must lie inside a weight row; fp8 needs only 16-byte
   // row strides for TMA (the ragged last k-block is zero-filled).
   if (M < 0 || N <= 0 || K <= 0 || (K % (fmt == kFmtNF4 ? 64 : 16)) != 0) return DQ_ERR_SHAPE;
@@ -389,7 +454,7 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
   DeviceInfo* d = nullptr;
   int rc = current_device(&d);
   if (rc != DQ_OK) return rc;
-  const Plan p = make_plan(M, N, K, d->sms);
+  const Plan p = make_plan(M, N, K, d->sms, tp == nullptr);
   if (p.ws > 0 && (ws == nullptr || ws_bytes < p.ws || !aligned(ws, 16))) return DQ_ERR_WORKSPACE;
 
   CUtensorMap mx, mw;
@@ -414,15 +479,47 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
   a.splits = p.splits;
   a.kb_per_split = p.kb_per_split;
   a.fp8_scale = scale;
+  for (int r = 0; r < kMaxRanks; ++r) {
+    a.outs[r] = nullptr;
+    a.tp_flags[r] = nullptr;
+  }
+  a.tp_counter = nullptr;
+  a.tp_rank = 0;
+  a.tp_epoch = 0;
+  a.out = nullptr;
   if (p.splits > 1) {
     a.out = ws;
     a.vec_ok = (N % 4 == 0) && aligned(ws, 16);
-  } else {
-    a.out = y;
+    a.n_out = 0;
+    a.ldy = static_cast<int>(N);
+    a.col0 = 0;
+  } else if (tp == nullptr) {
+    a.outs[0] = y;
+    a.n_out = 1;
+    a.ldy = static_cast<int>(N);
+    a.col0 = 0;
     a.vec_ok = (N % 8 == 0) && aligned(y, 16);
+  } else {
+    a.n_out = tp->world;
+    a.ldy = static_cast<int>(N * tp->world);
+    a.col0 = static_cast<int>(N * tp->rank);
+    a.vec_ok = (N % 8 == 0);
+    for (int r = 0; r < tp->world; ++r) {
+      a.outs[r] = tp->y_ranks[r];
+      a.tp_flags[r] = tp->flag_ranks[r];
+      a.vec_ok = a.vec_ok && aligned(tp->y_ranks[r], 16);
+    }
+    a.tp_counter = tp->counter;
+    a.tp_rank = tp->rank;
+    a.tp_epoch = tp->epoch;
   }
-  rc = fmt == kFmtNF4 ? dispatch_gemm<kFmtNF4>(d, p, mx, mw, a, st)
-                      : dispatch_gemm<kFmtFP8>(d, p, mx, mw, a, st);
+  if (tp == nullptr) {
+    rc = fmt == kFmtNF4 ? dispatch_gemm<kFmtNF4, false>(d, p, mx, mw, a, st)
+                        : dispatch_gemm<kFmtFP8, false>(d, p, mx, mw, a, st);
+  } else {
+    rc = fmt == kFmtNF4 ? dispatch_gemm<kFmtNF4, true>(d, p, mx, mw, a, st)
+                        : dispatch_gemm<kFmtFP8, true>(d, p, mx, mw, a, st);
+  }
   if (rc != DQ_OK) return rc;
   if (p.splits > 1) {
     const int64_t total = M * N;
@@ -431,7 +528,29 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
         static_cast<__nv_bfloat16*>(y));
     if (cudaGetLastError() != cudaSuccess) return DQ_ERR_LAUNCH;
   }
+  if (tp != nullptr) {
+    tp_wait_kernel<<<1, 32, 0, st>>>(tp->flag_ranks[tp->rank], tp->world, tp->epoch, kTpWaitNs);
+    if (cudaGetLastError() != cudaSuccess) return DQ_ERR_LAUNCH;
+  }
   return DQ_OK;
+}
+
+static int tp_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8_t* w,
+                   const float* absmax, float scale, const void* bias, int64_t N, int rank,
+                   int world, void* const* y_ranks, unsigned int* const* flag_ranks,
+                   unsigned int* counter, unsigned int epoch, cudaStream_t st) {
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world) return DQ_ERR_ARG;
+  if (y_ranks == nullptr || flag_ranks == nullptr || counter == nullptr) return DQ_ERR_ARG;
+  if (N <= 0 || (N % world) != 0) return DQ_ERR_SHAPE;
+  for (int r = 0; r < world; ++r) {
+    if (y_ranks[r] == nullptr || flag_ranks[r] == nullptr) return DQ_ERR_ARG;
+    if (!aligned(y_ranks[r], 2) || !aligned(flag_ranks[r], 4)) return DQ_ERR_ALIGN;
+  }
+  if (!aligned(counter, 4)) return DQ_ERR_ALIGN;
+  if (M == 0) return DQ_OK;
+  TpOpts tp{rank, world, y_ranks, flag_ranks, counter, epoch};
+  return linear_impl(fmt, x, M, K, w, absmax, scale, bias, N / world, y_ranks[rank], nullptr, 0,
+                     st, &tp);
 }
 
 }  // namespace dq
@@ -556,7 +675,14 @@ int dq_plan_info(int64_t M, int64_t N, int64_t K, int fmt, int* pair, int* bm, i
   *pair = p.pair ? 1 : 0;
   *bm = p.bm;
   *splits = p.splits;
-  *grid = p.pair ? 2 * p.grid : p.grid;
+  *grid = p.grid;
+  if (p.pair) {
+    int cap = 0;
+    const int prc = fmt == DQ_FMT_NF4 ? pair_capacity<kFmtNF4>(d, p.bm, &cap)
+                                      : pair_capacity<kFmtFP8>(d, p.bm, &cap);
+    if (prc != DQ_OK) return prc;
+    *grid = 2 * std::max(1, std::min(p.grid, cap));
+  }
   return DQ_OK;
 }
 
@@ -612,6 +738,59 @@ int dq_linear_nf4_noalloc(const void* x, int64_t M, int64_t K, const uint8_t* pa
   }
   return linear_impl(kFmtNF4, x, M, K, packed, absmax, 0.f, bias, N, y, scratch,
                      DQ_NOALLOC_SCRATCH_BYTES, static_cast<cudaStream_t>(stream));
+}
+
+int dq_tp_buffer_alloc(size_t bytes, void** ptr) {
+  if (ptr == nullptr || bytes == 0) return DQ_ERR_ARG;
+  *ptr = nullptr;
+  if (cudaMalloc(ptr, bytes) != cudaSuccess) return DQ_ERR_CUDA;
+  if (cudaMemset(*ptr, 0, bytes) != cudaSuccess) return DQ_ERR_CUDA;
+  return DQ_OK;
+}
+
+int dq_tp_buffer_free(void* ptr) {
+  if (ptr == nullptr) return DQ_OK;
+  return cudaFree(ptr) == cudaSuccess ? DQ_OK : DQ_ERR_CUDA;
+}
+
+int dq_ipc_handle(const void* ptr, void* handle_out) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == DQ_IPC_HANDLE_BYTES, "IPC handle size");
+  if (ptr == nullptr || handle_out == nullptr) return DQ_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, const_cast<void*>(ptr)) != cudaSuccess) return DQ_ERR_CUDA;
+  std::memcpy(handle_out, &h, sizeof(h));
+  return DQ_OK;
+}
+
+int dq_ipc_open(const void* handle, void** ptr) {
+  if (handle == nullptr || ptr == nullptr) return DQ_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  *ptr = nullptr;
+  if (cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+    return DQ_ERR_CUDA;
+  return DQ_OK;
+}
+
+int dq_ipc_close(void* ptr) {
+  if (ptr == nullptr) return DQ_OK;
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? DQ_OK : DQ_ERR_CUDA;
+}
+
+int dq_tp_linear_nf4(const void* x, int64_t M, int64_t K, const uint8_t* packed_shard,
+                     const float* absmax_shard, const void* bias_shard, int64_t N, int rank,
+                     int world, void* const* y_ranks, unsigned int* const* flag_ranks,
+                     unsigned int* counter, unsigned int epoch, dq_stream_t stream) {
+  return tp_impl(kFmtNF4, x, M, K, packed_shard, absmax_shard, 0.f, bias_shard, N, rank, world,
+                 y_ranks, flag_ranks, counter, epoch, static_cast<cudaStream_t>(stream));
+}
+
+int dq_tp_linear_fp8(const void* x, int64_t M, int64_t K, const uint8_t* w8_shard, float scale,
+                     const void* bias_shard, int64_t N, int rank, int world, void* const* y_ranks,
+                     unsigned int* const* flag_ranks, unsigned int* counter, unsigned int epoch,
+                     dq_stream_t stream) {
+  return tp_impl(kFmtFP8, x, M, K, w8_shard, nullptr, scale, bias_shard, N, rank, world, y_ranks,
+                 flag_ranks, counter, epoch, static_cast<cudaStream_t>(stream));
 }
 
 int dq_device_error(int* code, dq_stream_t stream) {

@@ -50,7 +50,14 @@ __device__ unsigned int g_dq_error = 0;
 // g_dq_trace[slot][index].
 #ifdef DQ_TRACE
 constexpr int kTraceLen = 4096;
-__device__ long long g_dq_trace[16][kTraceLen];
+constexpr int kTraceSlots = 32;  // 0-4 producers/MMA, 5+5g..9+5g dequant group g, 25
+__device__ long long g_dq_trace[kTraceSlots][kTraceLen];
+// Per CTA: globaltimer at start and end, and the SM it ran on.
+__device__ unsigned long long g_dq_cta_trace[1024][3];
+#define DQ_TRACE_CTA(field, value)                                                 \
+  do {                                                                             \
+    if (threadIdx.x == 0 && blockIdx.x < 1024) g_dq_cta_trace[blockIdx.x][field] = (value); \
+  } while (0)
 #define DQ_TRACE_POINT(slot, idx)                                   \
   do {                                                              \
     if (blockIdx.x == 0 && (idx) < kTraceLen) g_dq_trace[slot][idx] = clock64(); \
@@ -59,19 +66,59 @@ __device__ long long g_dq_trace[16][kTraceLen];
 #define DQ_TRACE_POINT(slot, idx) \
   do {                            \
   } while (0)
+#define DQ_TRACE_CTA(field, value) \
+  do {                             \
+  } while (0)
 #endif
+
+constexpr int kMaxRanks = 8;  // column-parallel ranks one launch can write to
 
 struct GemmArgs {
   const float* absmax;        // NF4: [N, K/64] f32 block scales
   const __nv_bfloat16* bias;  // [N] or nullptr
-  void* out;                  // bf16 Y [M, N] (splits == 1) or f32 partials [splits, M, N]
+  void* out;                  // f32 partials [splits, M, N] when splits > 1
   int M, N, K;
   int num_n_tiles, num_tiles;
   int tile_n;                 // weight rows per tile: 128 (one CTA) or 256 (CTA pair)
   int splits, kb_per_split;
   float fp8_scale;            // fp8: per-tensor scale (rounded to bf16 in-kernel)
-  int vec_ok;                 // 16-byte vector stores are aligned for `out`
+  int vec_ok;                 // 16-byte vector stores are aligned for every destination
+  // bf16 Y destinations (splits == 1): element (m, n) goes to
+  // outs[d][m * ldy + col0 + n] for every d < n_out.  One destination with
+  // ldy = N, col0 = 0 normally; every rank's y [M, N_total] (possibly peer
+  // memory) in the column-parallel linear.
+  void* outs[kMaxRanks];
+  int n_out, ldy, col0;
+  // Column-parallel completion: when tp_counter != nullptr every CTA fences
+  // its stores system-wide and counts itself done; the last one raises flag
+  // tp_rank of every rank's flag array (tp_flags[d]) to tp_epoch.
+  unsigned int* tp_counter;
+  unsigned int* tp_flags[kMaxRanks];
+  int tp_rank;
+  unsigned int tp_epoch;
 };
+
+// Column-parallel completion signal (every thread of the CTA calls it after
+// the teardown barrier; the epilogue threads have already fenced their stores
+// system-wide).
+__device__ __forceinline__ void tp_signal_done(const GemmArgs& a) {
+  if (a.tp_counter == nullptr || threadIdx.x != 0) return;
+  __threadfence();  // this CTA's error-word update precedes its count
+  const unsigned int done = atomicAdd(a.tp_counter, 1u);
+  if (done != gridDim.x - 1) return;
+  __threadfence();  // ... and is seen by the last CTA after it reads the count
+  *a.tp_counter = 0u;  // ready for the next launch (stream-ordered)
+  // A CTA that gave up on a wait left its tiles unwritten: raise no flag, so
+  // the other ranks' bounded waits report the failure too.
+  if (atomicOr(&g_dq_error, 0u) & (1u << kErrTimeout)) return;
+  __threadfence_system();
+#pragma unroll
+  for (int d = 0; d < kMaxRanks; ++d)
+    if (d < a.n_out)
+      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.tp_flags[d] + a.tp_rank),
+                   "r"(a.tp_epoch)
+                   : "memory");
+}
 
 template <int FMT, int BM>
 struct GemmCfg {
@@ -189,7 +236,7 @@ __device__ __forceinline__ float load_absmax(const GemmArgs& a, const RoundCurso
   return __ldg(a.absmax + static_cast<size_t>(n) * KB + kb);
 }
 
-template <int FMT, int BM>
+template <int FMT, int BM, bool TP>
 __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
     dq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x,
                    const __grid_constant__ CUtensorMap tmap_w, const GemmArgs args) {
@@ -254,6 +301,7 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  DQ_TRACE_CTA(0, globaltimer_ns());
 
   if (warp == C::kWProducerWarp) {
     // ----------------------------------------------------- weight producer
@@ -425,7 +473,7 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) mbar_arrive(wempty_bar(ws));
-          if (tp && group == 0) DQ_TRACE_POINT(15, q * R + j);
+          if (tp && group == 0) DQ_TRACE_POINT(25, q * R + j);
           uint32_t out[32];
           const uint32_t* pw = reinterpret_cast<const uint32_t*>(pk);
           if constexpr (FMT == kFmtNF4) {
@@ -518,14 +566,16 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
         const uint32_t* vc = v[c & 1];
         const int mrow0 = m0 + EC * c;  // token of staging row 0
         if (!f32_out) {
-          // stage [EC tokens][32 outputs] bf16, then write 64-byte row segments
+          // stage [EC tokens][32 outputs] bf16 per warp, then write 64-byte
+          // row segments of Y (to every rank's y in the column-parallel
+          // instantiation; the store loop is compiled only there: even an
+          // untaken one costs ~10% at BM=256, where the drain is exposed)
           __nv_bfloat16* sb = reinterpret_cast<__nv_bfloat16*>(stg);
 #pragma unroll
           for (int j = 0; j < EC; ++j)
             sts16(stg_s + 2u * (j * 32 + lane),
                   __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(vc[j]) + bias)));
           __syncwarp();
-          __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(args.out);
 #pragma unroll
           for (int i = 0; i < EC / 8; ++i) {
             const int row = (lane >> 2) + 8 * i;
@@ -533,13 +583,27 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
             const int m = mrow0 + row;
             const int nc = ncol0 + col;
             if (m < args.M) {
-              __nv_bfloat16* dst = y + static_cast<size_t>(m) * args.N + nc;
-              const __nv_bfloat16* src = sb + row * 32 + col;
+              const size_t off = TP ? static_cast<size_t>(m) * args.ldy + args.col0 + nc
+                                    : static_cast<size_t>(m) * args.N + nc;
               if (args.vec_ok && nc + 8 <= args.N) {
-                *reinterpret_cast<uint4*>(dst) = lds128(stg_s + 2u * (row * 32 + col));
+                const uint4 v16 = lds128(stg_s + 2u * (row * 32 + col));
+                if constexpr (TP) {
+#pragma unroll
+                  for (int d = 0; d < kMaxRanks; ++d)
+                    if (d < args.n_out)
+                      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.outs[d]) + off) = v16;
+                } else {
+                  *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.outs[0]) + off) = v16;
+                }
               } else {
-                for (int e = 0; e < 8; ++e)
-                  if (nc + e < args.N) dst[e] = src[e];
+                const __nv_bfloat16* src = sb + row * 32 + col;
+#pragma unroll
+                for (int d = 0; d < (TP ? kMaxRanks : 1); ++d) {
+                  if (d >= args.n_out) break;
+                  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.outs[d]) + off;
+                  for (int e = 0; e < 8; ++e)
+                    if (nc + e < args.N) dst[e] = src[e];
+                }
               }
             }
           }
@@ -575,6 +639,9 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
       }
       if (++acc == C::kNumAcc) { acc = 0; accphase ^= 1u; }
     }
+    // Column-parallel output: this thread's peer stores are visible system-wide
+    // before its CTA counts itself done.
+    if constexpr (TP) __threadfence_system();
   }
 
   // ------------------------------------------------------------- teardown
@@ -583,6 +650,15 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
   tc_fence_after();
   if (warp == C::kMmaWarp) tmem_dealloc(tmem_base, 512);
   if (threadIdx.x == 0 && *abort_flag) atomicOr(&g_dq_error, 1u << kErrTimeout);
+  if constexpr (TP) tp_signal_done(args);
+#ifdef DQ_TRACE
+  {
+    unsigned int smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    DQ_TRACE_CTA(1, globaltimer_ns());
+    DQ_TRACE_CTA(2, smid);
+  }
+#endif
 }
 
 }  // namespace dq

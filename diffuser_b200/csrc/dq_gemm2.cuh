@@ -80,7 +80,7 @@ struct Gemm2Cfg {
   static constexpr uint32_t kXTxBytes = BM * 128;               // both halves of a k-block
 };
 
-template <int FMT, int BM>
+template <int FMT, int BM, bool TP>
 __global__ void __launch_bounds__(Gemm2Cfg<FMT, BM>::kThreads, 1)
     dq_gemm2_kernel(const __grid_constant__ CUtensorMap tmap_x,
                     const __grid_constant__ CUtensorMap tmap_w, const GemmArgs args) {
@@ -150,6 +150,7 @@ __global__ void __launch_bounds__(Gemm2Cfg<FMT, BM>::kThreads, 1)
   cluster_sync();  // both CTAs' barriers exist before anyone signals across the pair
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  DQ_TRACE_CTA(0, globaltimer_ns());
 
   if (warp == C::kWProducerWarp) {
     // ----------------------------------------------------- weight producer
@@ -405,13 +406,16 @@ __global__ void __launch_bounds__(Gemm2Cfg<FMT, BM>::kThreads, 1)
         const uint32_t* vc = v[c & 1];
         const int mrow0 = m0 + EC * c;
         if (!f32_out) {
+          // stage [EC tokens][32 outputs] bf16 per warp, then write 64-byte
+          // row segments of Y (to every rank's y in the column-parallel
+          // instantiation; the store loop is compiled only there: even an
+          // untaken one costs ~10% at BM=256, where the drain is exposed)
           __nv_bfloat16* sb = reinterpret_cast<__nv_bfloat16*>(stg);
 #pragma unroll
           for (int j = 0; j < EC; ++j)
             sts16(stg_s + 2u * (j * 32 + lane),
                   __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(vc[j]) + bias)));
           __syncwarp();
-          __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(args.out);
 #pragma unroll
           for (int i = 0; i < EC / 8; ++i) {
             const int row = (lane >> 2) + 8 * i;
@@ -419,13 +423,27 @@ __global__ void __launch_bounds__(Gemm2Cfg<FMT, BM>::kThreads, 1)
             const int m = mrow0 + row;
             const int nc = ncol0 + col;
             if (m < args.M) {
-              __nv_bfloat16* dst = y + static_cast<size_t>(m) * args.N + nc;
-              const __nv_bfloat16* src = sb + row * 32 + col;
+              const size_t off = TP ? static_cast<size_t>(m) * args.ldy + args.col0 + nc
+                                    : static_cast<size_t>(m) * args.N + nc;
               if (args.vec_ok && nc + 8 <= args.N) {
-                *reinterpret_cast<uint4*>(dst) = lds128(stg_s + 2u * (row * 32 + col));
+                const uint4 v16 = lds128(stg_s + 2u * (row * 32 + col));
+                if constexpr (TP) {
+#pragma unroll
+                  for (int d = 0; d < kMaxRanks; ++d)
+                    if (d < args.n_out)
+                      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.outs[d]) + off) = v16;
+                } else {
+                  *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.outs[0]) + off) = v16;
+                }
               } else {
-                for (int e = 0; e < 8; ++e)
-                  if (nc + e < args.N) dst[e] = src[e];
+                const __nv_bfloat16* src = sb + row * 32 + col;
+#pragma unroll
+                for (int d = 0; d < (TP ? kMaxRanks : 1); ++d) {
+                  if (d >= args.n_out) break;
+                  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.outs[d]) + off;
+                  for (int e = 0; e < 8; ++e)
+                    if (nc + e < args.N) dst[e] = src[e];
+                }
               }
             }
           }
@@ -460,6 +478,9 @@ __global__ void __launch_bounds__(Gemm2Cfg<FMT, BM>::kThreads, 1)
       }
       if (++acc == C::kNumAcc) { acc = 0; accphase ^= 1u; }
     }
+    // Column-parallel output: this thread's peer stores are visible system-wide
+    // before its CTA counts itself done.
+    if constexpr (TP) __threadfence_system();
   }
 
   // ------------------------------------------------------------- teardown
@@ -469,6 +490,15 @@ __global__ void __launch_bounds__(Gemm2Cfg<FMT, BM>::kThreads, 1)
   tc_fence_after();
   if (warp == C::kMmaWarp) tmem_dealloc_pair(tmem_base, 512);
   if (threadIdx.x == 0 && *abort_flag) atomicOr(&g_dq_error, 1u << kErrTimeout);
+  if constexpr (TP) tp_signal_done(args);
+#ifdef DQ_TRACE
+  {
+    unsigned int smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    DQ_TRACE_CTA(1, globaltimer_ns());
+    DQ_TRACE_CTA(2, smid);
+  }
+#endif
 }
 
 }  // namespace dq

@@ -133,6 +133,43 @@ int dq_set_tile_override(int bm, int splits);
  * tile (128 weight rows), 2 = CTA-pair tiles (256 weight rows, x-tile >= 64). */
 int dq_set_pair_mode(int mode);
 
+/* ------------------------------------------------- column-parallel linear
+ * Tensor parallelism over out_features for one linear (the weight rows split
+ * across `world` GPUs of one node, 1 <= world <= 8).  Rank r holds weight rows
+ * [r*N/world, (r+1)*N/world): for NF4 the byte range [n0*K/2, n1*K/2) of the
+ * reference's packed buffer and [n0*K/64, n1*K/64) of absmax (NF4 blocks are
+ * row-local, so a shard needs no repacking), for fp8 those rows of w8 with the
+ * shared scalar scale.  Each rank's fused kernel stores its [M, N/world]
+ * block straight into EVERY rank's y [M, N] (bf16, columns n0..n1) through
+ * peer pointers, then raises its flag in every rank's flag array; the call
+ * enqueues a bounded wait (5 s, then DQ_ERR_TIMEOUT in dq_device_error) until
+ * this rank's flags show all blocks have landed.  No library collective.
+ *
+ *   y_ranks[world]    host array of device pointers: rank q's y, mapped here
+ *   flag_ranks[world] host array of device pointers: rank q's uint32[world]
+ *   counter           this rank's uint32, zero before the first call
+ *   epoch             1, 2, 3, ... one per call, the same on every rank
+ *
+ * Buffers shared between ranks come from dq_tp_buffer_alloc (zero-filled) and
+ * are mapped into the other processes with dq_ipc_handle / dq_ipc_open.
+ * N % world == 0.  One call in flight per device.  The reference has no
+ * multi-GPU path; this is the partitioning of its linear (R/nf4_ltx23.R:235-246,
+ * R/fp8_ltx23.R:70-83) over rows of W. */
+#define DQ_IPC_HANDLE_BYTES 64
+int dq_tp_buffer_alloc(size_t bytes, void** ptr);
+int dq_tp_buffer_free(void* ptr);
+int dq_ipc_handle(const void* ptr, void* handle_out);
+int dq_ipc_open(const void* handle, void** ptr);
+int dq_ipc_close(void* ptr);
+int dq_tp_linear_nf4(const void* x, int64_t M, int64_t K, const uint8_t* packed_shard,
+                     const float* absmax_shard, const void* bias_shard, int64_t N, int rank,
+                     int world, void* const* y_ranks, unsigned int* const* flag_ranks,
+                     unsigned int* counter, unsigned int epoch, dq_stream_t stream);
+int dq_tp_linear_fp8(const void* x, int64_t M, int64_t K, const uint8_t* w8_shard, float scale,
+                     const void* bias_shard, int64_t N, int rank, int world, void* const* y_ranks,
+                     unsigned int* const* flag_ranks, unsigned int* counter, unsigned int epoch,
+                     dq_stream_t stream);
+
 /* Describes the launch plan dq_linear_* uses for this shape on the current
  * device: *pair = 1 for CTA-pair tiles (256 weight rows per tile) or 0 for
  * one-CTA tiles (128 rows), *bm = x-tile rows, *splits = split-K count,
