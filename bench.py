@@ -53,7 +53,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["tp_fp8"], default="nf4")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["tp_fp8", "flux_dit"], default="nf4")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
@@ -505,19 +505,111 @@ def run_tp(args, world, rank, local):
     dist.destroy_process_group()
 
 
+# ------------------------------------------------------------ FLUX DiT step
+def run_flux(args, world, rank, local):
+    """One flow-match Euler step of the FLUX.1 transformer at 1024x1024 (4096
+    image + 512 text tokens) with its 494 cast linears in NF4 on the fused
+    engine, one image per GPU (latent seed 10 + rank).  Also times the same
+    step with the reference's linear algorithm (dequantize each NF4 weight
+    into a per-shape bf16 buffer, then cuBLAS) on the same model and box."""
+    import torch.distributed as dist
+    from diffuser_b200 import flux, modules, ops
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    model = flux.build_flux_nf4(dev, seed=0)
+    g = torch.Generator().manual_seed(10 + rank)
+    x = flux.pack_latents(torch.randn(1, 16, 128, 128, generator=g)).to(dev, torch.bfloat16)
+    g1 = torch.Generator().manual_seed(3)
+    text = torch.randn(1, 512, 4096, generator=g1).to(dev, torch.bfloat16)
+    pooled = torch.randn(1, 768, generator=g1).to(dev, torch.bfloat16)
+    ids = torch.cat([torch.zeros(512, 3), flux.prepare_latent_image_ids(64, 64)], dim=0)
+    rope = flux.pos_embed(ids.to(dev), (16, 56, 56))
+    t = torch.ones(1, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        with torch.no_grad():
+            v = model(x, text, pooled, t, rope)
+            return flux.euler_step(v, 1.0, 0.75, x)
+
+    def timed(steps):
+        for _ in range(max(args.warmup, 3)):
+            step()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world)
+        torch.cuda.synchronize()
+        a.record(stream)
+        for _ in range(steps):
+            step()
+        b.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        return max_over_ranks(a.elapsed_time(b) / steps, world, dev)
+
+    with ClockSampler(local) as clk:
+        ms = timed(args.steps)
+    err = ops.device_error(dev)
+    # the reference's algorithm for every NF4 linear, same weights
+    nf4 = [m for m in model.modules() if isinstance(m, modules.Ltx23Nf4Linear)]
+    bufs = {}
+    saved = []
+    for m in nf4:
+        key = (m.out_features, m.in_features)
+        if key not in bufs:
+            bufs[key] = torch.empty(key, dtype=torch.bfloat16, device=dev)
+
+        def fwd(xx, m=m, buf=bufs[key]):
+            ops.ltx23_nf4_dequantize(m.weight_nf4, m.weight_absmax, buf.shape, out=buf)
+            return torch.nn.functional.linear(xx, buf, m.bias)
+        saved.append((m, m.forward))
+        m.forward = fwd
+    ref_ms = timed(max(3, args.steps // 2))
+    for m, f in saved:
+        m.forward = f
+    if rank == 0:
+        cast_flops = 59.50e12  # cast linears per step at 1024x1024, B = 1
+        line = {
+            "metric": "FLUX.1 1024x1024 DiT step ms", "value": ms, "unit": "ms", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random N(0,0.02) weights, NF4 cast linears)",
+            "config": {"workload": "FLUX.1 transformer, 19 double + 38 single blocks, 4096 image + 512 text "
+                                   "tokens, one Euler step, one image per GPU",
+                       "parallelism": f"dp{world} (replicas, no collective)"},
+            "images_per_s_4_steps": world / (4 * ms * 1e-3),
+            "cast_linear_tflops_if_all_time": cast_flops / (ms * 1e-3) / 1e12,
+            "reference_algorithm_step_ms": ref_ms,
+            "speedup_vs_reference_algorithm": ref_ms / ms,
+            "device_error": err, "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
-        if args.workload == "tp_fp8":
+        if args.workload in ("tp_fp8", "flux_dit"):
             if rank == 0:
-                print(json.dumps({"impl": "reference", "unavailable":
-                                  "the reference runs each linear on one GPU; it has no column-parallel path"}))
+                why = ("the reference runs each linear on one GPU; it has no column-parallel path"
+                       if args.workload == "tp_fp8" else
+                       "the reference's FLUX step runs in R (not installed); its GPU linear algorithm "
+                       "is timed inside the flux_dit line (reference_algorithm_step_ms)")
+                print(json.dumps({"impl": "reference", "unavailable": why}))
             return
         run_reference_arm(args, world, rank)
         return
     if args.workload == "tp_fp8":
         run_tp(args, world, rank, local)
+        return
+    if args.workload == "flux_dit":
+        run_flux(args, world, rank, local)
         return
     run_ours(args, world, rank, local)
 

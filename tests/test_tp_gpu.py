@@ -92,3 +92,44 @@ def test_column_parallel_matches_single_gpu(tmp_path):
                 assert m == 0, table
                 continue
             assert fused_equal and nccl_equal, table
+
+
+def _timeout_rank(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    from diffuser_b200 import ops, tp
+    grp = tp.TpGroup(max_tokens=64, max_out_features=256)
+    code = -1
+    try:
+        w = torch.randn(256, 128, device="cuda") * 0.02
+        w8, s = ops.fp8_quantize(w)
+        mod = tp.ColumnParallelFp8Linear(128, 256, grp, bias=False).cuda()
+        mod.set_fp8_weight(w8, float(s.item()))
+        x = torch.randn(16, 128, device="cuda").to(torch.bfloat16)
+        ops.device_error()  # clear
+        dist.barrier()
+        if rank == 0:
+            # the peers skip this call: their flags never reach this epoch, so
+            # the bounded wait runs out and records a timeout (no fault, no hang)
+            mod(x)
+            torch.cuda.synchronize()
+        code = ops.device_error()
+        dist.barrier()
+    finally:
+        grp.close()
+        dist.destroy_process_group()
+    np.save(os.path.join(out_dir, f"timeout_{rank}.npy"), np.array([code]))
+
+
+def test_column_parallel_wait_times_out_when_a_rank_is_missing(tmp_path):
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("needs at least two GPUs")
+    from diffuser_b200 import _lib
+    mp.start_processes(_timeout_rank, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    assert int(np.load(tmp_path / "timeout_0.npy")[0]) == _lib.DQ_ERR_TIMEOUT
+    for r in range(1, world):
+        assert int(np.load(tmp_path / f"timeout_{r}.npy")[0]) == 0
