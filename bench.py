@@ -61,18 +61,20 @@ def parse():
 
 # ------------------------------------------------------------------- peaks
 def measured_peaks():
+    """(burst bf16 TFLOP/s, sustained bf16 TFLOP/s, HBM GB/s, source)."""
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
         with open(path) as f:
             d = json.load(f)
-        return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
+        return (float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                float(d["hbm_gbs"]), "measured")
     except Exception:
-        return 1590.0, 6650.0, "fallback"
+        return 1590.0, 1400.0, 6650.0, "fallback"
 
 
-def profile_traffic(workload: str, pair: bool):
+def profile_traffic(workload: str, plan: dict):
     """DRAM bytes per launch of the planned kernel from its committed ncu summary."""
-    kern = "dq_gemm2" if pair else "dq_gemm"
+    kern = "bf16_gemm2" if plan["twophase"] else ("dq_gemm2" if plan["pair"] else "dq_gemm")
     path = os.path.join(ROOT, "profiles", f"{kern}_{workload}_4608x3072x12288.md")
     try:
         txt = open(path).read()
@@ -286,7 +288,9 @@ def run_ours(args, world, rank, local):
     ws_bytes = ops.workspace_size(M, N, K, 0 if fmt == "nf4" else 1)
     ws = ops.workspace(dev, ws_bytes)
     wsp = ctypes.c_void_p(ws.data_ptr()) if ws is not None else None
-    launches_per_step = 1 + (1 if ws_bytes > 0 else 0)
+    plan0 = ops.plan_info(M, N, K, 0 if fmt == "nf4" else 1)
+    # two-phase: dequantize + bf16 GEMM; split-K: GEMM + reduce; else one kernel
+    launches_per_step = 2 if (plan0["twophase"] or plan0["splits"] > 1) else 1
 
     def launch(i):
         x, y = xs[i % ROTATE], ys[i % ROTATE]
@@ -398,10 +402,10 @@ def run_ours(args, world, rank, local):
                          "overlapped across consecutive steps"}
 
     if rank == 0:
-        peak_tf, peak_bw, peak_src = measured_peaks()
+        burst_tf, peak_tf, peak_bw, peak_src = measured_peaks()
         achieved = FLOPS_PER_STEP / (kern_ms_max * 1e-3) / 1e12
         plan = ops.plan_info(M, N, K, 0 if fmt == "nf4" else 1)
-        traffic = profile_traffic(fmt, plan["pair"])
+        traffic = profile_traffic(fmt, plan)
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             cpu = run_cpu_baseline(fmt)
@@ -414,9 +418,12 @@ def run_ours(args, world, rank, local):
             "config": {"workload": WORKLOADS[fmt]["desc"], "format": fmt, "M": M, "N": N, "K": K,
                        "bias": False, "parallelism": f"dp{world} (own token batch per GPU, replicated weight, no collective)",
                        "l2": f"{ROTATE} rotating input sets ({ROTATE * WORKLOADS[fmt]['bytes'] / 1e6:.0f} MB) > 126 MB L2"},
+            # the timed region is hundreds of launches back to back, under the
+            # 1000 W cap: the sustained bf16 figure is the denominator
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": achieved / peak_tf, "traffic": traffic,
-                         "peak_source": f"{peak_src} bf16 dense (burst)",
+                         "peak_source": f"{peak_src} bf16 dense, sustained (back-to-back loop)",
+                         "frac_of_burst_peak": achieved / burst_tf,
                          "kernel": f"{plan['kernel']} {fmt} BM={plan['bm']}", "kernel_ms": kern_ms_max,
                          "kernel_ms_per_rank": kern_ms_ranks,
                          "algorithmic_bytes": WORKLOADS[fmt]["bytes"]},
@@ -485,7 +492,7 @@ def run_tp(args, world, rank, local):
     flops = 2 * TP_M * TP_N * TP_K
     peer_bytes = (world - 1) * TP_M * (TP_N // world) * 2  # sent by each rank
     if rank == 0:
-        peak_tf, _, peak_src = measured_peaks()
+        peak_tf, _, _, peak_src = measured_peaks()
         line = {
             "metric": "column-parallel fp8 linear TFLOP/s", "value": flops / (fused_ms * 1e-3) / 1e12,
             "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),

@@ -15,6 +15,7 @@
 #include "../../include/dq_linear.h"
 #include "dq_gemm.cuh"
 #include "dq_gemm2.cuh"
+#include "dq_bf16gemm2.cuh"
 
 #define DQ_VERSION_STRING "dqlinear-b200 0.1.0 (sm_100a)"
 
@@ -168,6 +169,8 @@ struct DeviceInfo {
   int smem_set[2][2][6] = {};   // [column-parallel][fmt][bm]
   int smem_set2[2][2][6] = {};
   int max_pairs[2][6] = {};     // [fmt][bm]
+  int bf16_smem_set[6] = {};    // bf16 pair GEMM, [bm]
+  int bf16_max_pairs[6] = {};
 };
 
 constexpr int kMaxDevices = 64;
@@ -225,7 +228,8 @@ static bool make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType 
 
 // ----------------------------------------------------------- launch plan
 struct Plan {
-  bool pair = false;  // CTA-pair kernel (256 weight rows per tile)
+  bool pair = false;      // CTA-pair tiles (256 weight rows per tile)
+  bool twophase = false;  // dequantize into bf16 scratch, then the bf16 pair GEMM
   int bm = 0, splits = 1, kb_per_split = 0;
   int m_tiles = 0, n_tiles = 0, tiles = 0, grid = 0;
   size_t ws = 0;
@@ -253,14 +257,38 @@ struct TileShape {
 static constexpr TileShape kShapes[] = {
     {false, 128, 0.72}, {false, 192, 1.0}, {false, 256, 0.97}, {true, 192, 0.93}, {true, 256, 1.13}};
 
-static Plan make_plan(int64_t M, int64_t N, int64_t K, int sms, bool allow_split = true) {
+// Token count from which the two-phase plan is chosen: decoding the weight
+// once (~N*K*2.6 bytes of HBM traffic) costs less than decoding it in every
+// token tile, and the bf16 pair GEMM runs faster than the fused kernels.
+constexpr int64_t kTwoPhaseMinM = 1024;
+
+static Plan make_plan(int64_t M, int64_t N, int64_t K, int sms, bool allow_split = true,
+                      bool allow_twophase = true) {
   Plan p;
   const int KB = static_cast<int>((K + 63) / 64);
-  const int opair = g_override_pair.load();  // 0 automatic, 1 one-CTA only, 2 pairs only
+  // 0 automatic, 1 one-CTA fused only, 2 CTA-pair fused only, 3 two-phase only
+  const int opair = g_override_pair.load();
   const int obm = g_override_bm.load();
   auto units_of = [&](bool pair) { return pair ? sms / 2 : sms; };
   auto n_tiles_of = [&](bool pair) { return static_cast<int>((N + (pair ? 255 : 127)) / (pair ? 256 : 128)); };
-  if (opair == 2 && M > 64) {
+  const bool twophase = allow_twophase && M > 64 &&
+                        (opair == 3 || (opair == 0 && M >= kTwoPhaseMinM));
+  if (twophase) {
+    p.pair = true;
+    p.twophase = true;
+    if (obm >= 64 && bm_index(obm) >= 0) {
+      p.bm = obm;
+    } else {
+      // fewest waves of 256-row tiles, preferring the taller x tile on ties
+      p.bm = 256;
+      double best = 1e30;
+      for (int bm : {256, 192, 128}) {
+        const int64_t tiles = ((M + bm - 1) / bm) * n_tiles_of(true);
+        const double cost = static_cast<double>((tiles + units_of(true) - 1) / units_of(true)) * bm;
+        if (cost < best - 1e-9) { best = cost; p.bm = bm; }
+      }
+    }
+  } else if (opair == 2 && M > 64) {
     p.pair = true;
     p.bm = (obm >= 64 && bm_index(obm) >= 0) ? obm : 256;
   } else if (obm > 0 && bm_index(obm) >= 0) {
@@ -299,15 +327,16 @@ static Plan make_plan(int64_t M, int64_t N, int64_t K, int sms, bool allow_split
   const int os = g_override_splits.load();
   if (os > 0) {
     s = os;
-  } else if (allow_split && base_tiles * 2 <= units && KB >= 8) {
+  } else if (allow_split && !p.twophase && base_tiles * 2 <= units && KB >= 8) {
     s = std::min(std::min(units / base_tiles, KB / 4), 16);
   }
-  s = allow_split ? std::max(1, std::min(s, KB)) : 1;
+  s = (allow_split && !p.twophase) ? std::max(1, std::min(s, KB)) : 1;
   p.kb_per_split = (KB + s - 1) / s;
   p.splits = (KB + p.kb_per_split - 1) / p.kb_per_split;
   p.tiles = base_tiles * p.splits;
   p.grid = std::min(p.tiles, units);  // CTAs (1-CTA kernel) or pairs (pair kernel)
   p.ws = p.splits > 1 ? static_cast<size_t>(p.splits) * M * N * sizeof(float) : 0;
+  if (p.twophase) p.ws = static_cast<size_t>(N) * K * 2;  // the bf16 weight
   return p;
 }
 
@@ -393,6 +422,70 @@ static int pair_capacity(DeviceInfo* d, int bm, int* pairs) {
   return rc;
 }
 
+template <int BM>
+static cudaLaunchConfig_t bf16_pair_config(cudaLaunchAttribute* attr, cudaStream_t st) {
+  using C = Bf16PairCfg<BM>;
+  cudaLaunchConfig_t cfg = {};
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+// One-time setup of a bf16 pair GEMM instantiation: shared-memory opt-in and
+// the resident-cluster capacity (cached in d->bf16_max_pairs).
+template <int BM>
+static int bf16_pair_setup(DeviceInfo* d) {
+  using C = Bf16PairCfg<BM>;
+  const int bi = bm_index(BM);
+  if (d->bf16_smem_set[bi]) return DQ_OK;
+  auto kern = bf16_gemm2_kernel<BM>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
+      cudaSuccess)
+    return DQ_ERR_LAUNCH;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = bf16_pair_config<BM>(attr, nullptr);
+  cfg.gridDim = dim3(2 * std::max(1, d->sms / 2));
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1)
+    return DQ_ERR_LAUNCH;
+  d->bf16_max_pairs[bi] = clusters;
+  d->bf16_smem_set[bi] = 1;
+  return DQ_OK;
+}
+
+static int bf16_pair_capacity(DeviceInfo* d, int bm, int* pairs) {
+  int rc = DQ_ERR_ARG;
+  switch (bm) {
+    case 64: rc = bf16_pair_setup<64>(d); break;
+    case 128: rc = bf16_pair_setup<128>(d); break;
+    case 192: rc = bf16_pair_setup<192>(d); break;
+    case 256: rc = bf16_pair_setup<256>(d); break;
+  }
+  if (rc == DQ_OK) *pairs = d->bf16_max_pairs[bm_index(bm)];
+  return rc;
+}
+
+template <int BM>
+static int launch_bf16_gemm2(DeviceInfo* d, const Plan& p, const CUtensorMap& mx,
+                             const CUtensorMap& ma, const GemmArgs& a, cudaStream_t st) {
+  const int rc = bf16_pair_setup<BM>(d);
+  if (rc != DQ_OK) return rc;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = bf16_pair_config<BM>(attr, st);
+  const int pairs = std::max(1, std::min(p.grid, d->bf16_max_pairs[bm_index(BM)]));
+  cfg.gridDim = dim3(2 * pairs);
+  if (cudaLaunchKernelEx(&cfg, bf16_gemm2_kernel<BM>, mx, ma, a) != cudaSuccess)
+    return DQ_ERR_LAUNCH;
+  return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
+}
+
 template <int FMT, bool TP>
 static int dispatch_gemm(DeviceInfo* d, const Plan& p, const CUtensorMap& mx, const CUtensorMap& mw,
                          const GemmArgs& a, cudaStream_t st) {
@@ -440,7 +533,8 @@ static constexpr unsigned long long kTpWaitNs = 5000000000ull;  // 5 s
 
 static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8_t* w,
                        const float* absmax, float scale, const void* bias, int64_t N, void* y,
-                       void* ws, size_t ws_bytes, cudaStream_t st, const TpOpts* tp = nullptr) {
+                       void* ws, size_t ws_bytes, cudaStream_t st, const TpOpts* tp = nullptr,
+                       bool allow_twophase = true) {
   // NF4 blocks of 64 must lie inside a weight row; fp8 needs only 16-byte
   // row strides for TMA (the ragged last k-block is zero-filled).
   if (M < 0 || N <= 0 || K <= 0 || (K % (fmt == kFmtNF4 ? 64 : 16)) != 0) return DQ_ERR_SHAPE;
@@ -454,8 +548,61 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
   DeviceInfo* d = nullptr;
   int rc = current_device(&d);
   if (rc != DQ_OK) return rc;
-  const Plan p = make_plan(M, N, K, d->sms, tp == nullptr);
+  const Plan p = make_plan(M, N, K, d->sms, tp == nullptr, allow_twophase && tp == nullptr);
   if (p.ws > 0 && (ws == nullptr || ws_bytes < p.ws || !aligned(ws, 16))) return DQ_ERR_WORKSPACE;
+
+  if (p.twophase) {
+    // phase 1: the weight, dequantized once into the bf16 scratch [N, K]
+    const int64_t n_elems = N * K;
+    if (fmt == kFmtNF4) {
+      dequant_nf4_kernel<<<grid_for(n_elems / 32, 256, d->sms), 256, 0, st>>>(
+          reinterpret_cast<const uint4*>(w), absmax, static_cast<uint4*>(ws), n_elems / 32);
+    } else {
+      dequant_fp8_kernel<<<grid_for(n_elems / 16 + 1, 256, d->sms), 256, 0, st>>>(
+          w, scale, static_cast<__nv_bfloat16*>(ws), n_elems);
+    }
+    if (cudaGetLastError() != cudaSuccess) return DQ_ERR_LAUNCH;
+    // phase 2: bf16 x bf16 pair GEMM
+    CUtensorMap mx2, ma;
+    if (!make_map_2d(&mx2, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, M, K * 2, 64, p.bm / 2,
+                     CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map_2d(&ma, ws, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, N, K * 2, 64, 128,
+                     CU_TENSOR_MAP_SWIZZLE_128B))
+      return DQ_ERR_CUDA;
+    GemmArgs g;
+    g.absmax = nullptr;
+    g.bias = static_cast<const __nv_bfloat16*>(bias);
+    g.out = nullptr;
+    g.M = static_cast<int>(M);
+    g.N = static_cast<int>(N);
+    g.K = static_cast<int>(K);
+    g.num_n_tiles = p.n_tiles;
+    g.tile_n = 256;
+    g.num_tiles = p.tiles;
+    g.splits = 1;
+    g.kb_per_split = p.kb_per_split;
+    g.group_n = 16;  // the bf16 weight (N*K*2 bytes) no longer fits L2 beside X and Y
+    g.fp8_scale = 0.f;
+    for (int r = 0; r < kMaxRanks; ++r) {
+      g.outs[r] = nullptr;
+      g.tp_flags[r] = nullptr;
+    }
+    g.outs[0] = y;
+    g.n_out = 1;
+    g.ldy = static_cast<int>(N);
+    g.col0 = 0;
+    g.vec_ok = (N % 8 == 0) && aligned(y, 16);
+    g.tp_counter = nullptr;
+    g.tp_rank = 0;
+    g.tp_epoch = 0;
+    switch (p.bm) {
+      case 64: return launch_bf16_gemm2<64>(d, p, mx2, ma, g, st);
+      case 128: return launch_bf16_gemm2<128>(d, p, mx2, ma, g, st);
+      case 192: return launch_bf16_gemm2<192>(d, p, mx2, ma, g, st);
+      case 256: return launch_bf16_gemm2<256>(d, p, mx2, ma, g, st);
+    }
+    return DQ_ERR_ARG;
+  }
 
   CUtensorMap mx, mw;
   if (!make_map_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, M, K * 2, 64,
@@ -478,6 +625,7 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
   a.num_tiles = p.tiles;
   a.splits = p.splits;
   a.kb_per_split = p.kb_per_split;
+  a.group_n = 0;
   a.fp8_scale = scale;
   for (int r = 0; r < kMaxRanks; ++r) {
     a.outs[r] = nullptr;
@@ -672,11 +820,16 @@ int dq_plan_info(int64_t M, int64_t N, int64_t K, int fmt, int* pair, int* bm, i
   const int rc = current_device(&d);
   if (rc != DQ_OK) return rc;
   const Plan p = make_plan(M, N, K, d->sms);
-  *pair = p.pair ? 1 : 0;
+  *pair = p.twophase ? 2 : (p.pair ? 1 : 0);
   *bm = p.bm;
   *splits = p.splits;
   *grid = p.grid;
-  if (p.pair) {
+  if (p.twophase) {
+    int cap = 0;
+    const int prc = bf16_pair_capacity(d, p.bm, &cap);
+    if (prc != DQ_OK) return prc;
+    *grid = 2 * std::max(1, std::min(p.grid, cap));
+  } else if (p.pair) {
     int cap = 0;
     const int prc = fmt == DQ_FMT_NF4 ? pair_capacity<kFmtNF4>(d, p.bm, &cap)
                                       : pair_capacity<kFmtFP8>(d, p.bm, &cap);
@@ -721,7 +874,8 @@ int dq_linear_nf4_noalloc(const void* x, int64_t M, int64_t K, const uint8_t* pa
   DeviceInfo* d = nullptr;
   int rc = current_device(&d);
   if (rc != DQ_OK) return rc;
-  if (make_plan(M, N, K, d->sms).ws > DQ_NOALLOC_SCRATCH_BYTES) return DQ_ERR_SCRATCH_LIMIT;
+  if (make_plan(M, N, K, d->sms, true, false).ws > DQ_NOALLOC_SCRATCH_BYTES)
+    return DQ_ERR_SCRATCH_LIMIT;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return DQ_ERR_CUDA;
   void* scratch = g_noalloc_addr[dev].load();
@@ -737,7 +891,7 @@ int dq_linear_nf4_noalloc(const void* x, int64_t M, int64_t K, const uint8_t* pa
     }
   }
   return linear_impl(kFmtNF4, x, M, K, packed, absmax, 0.f, bias, N, y, scratch,
-                     DQ_NOALLOC_SCRATCH_BYTES, static_cast<cudaStream_t>(stream));
+                     DQ_NOALLOC_SCRATCH_BYTES, static_cast<cudaStream_t>(stream), nullptr, false);
 }
 
 int dq_tp_buffer_alloc(size_t bytes, void** ptr) {
@@ -807,7 +961,7 @@ int dq_device_error(int* code, dq_stream_t stream) {
 }
 
 int dq_set_pair_mode(int mode) {
-  if (mode < 0 || mode > 2) return DQ_ERR_ARG;
+  if (mode < 0 || mode > 3) return DQ_ERR_ARG;
   g_override_pair.store(mode);
   return DQ_OK;
 }

@@ -81,6 +81,7 @@ struct GemmArgs {
   int num_n_tiles, num_tiles;
   int tile_n;                 // weight rows per tile: 128 (one CTA) or 256 (CTA pair)
   int splits, kb_per_split;
+  int group_n;                // > 0: tiles visit group_n weight tiles x all token tiles at a time
   float fp8_scale;            // fp8: per-tensor scale (rounded to bf16 in-kernel)
   int vec_ok;                 // 16-byte vector stores are aligned for every destination
   // bf16 Y destinations (splits == 1): element (m, n) goes to
@@ -185,8 +186,21 @@ __device__ __forceinline__ TileCoord tile_coord(const GemmArgs& a, int t, int KB
   TileCoord c;
   c.split = t % a.splits;
   const int mn = t / a.splits;
-  c.n0 = (mn % a.num_n_tiles) * a.tile_n;
-  c.m0 = (mn / a.num_n_tiles);
+  if (a.group_n > 0) {
+    // Grouped order: token tiles run fastest over a group of group_n weight
+    // tiles, so the tiles in flight share a few weight tiles (kept in L2)
+    // instead of streaming every weight row once per token tile.
+    const int m_tiles = a.num_tiles / (a.splits * a.num_n_tiles);
+    const int per_group = a.group_n * m_tiles;
+    const int g = mn / per_group;
+    const int r = mn - g * per_group;
+    const int gn = min(a.group_n, a.num_n_tiles - g * a.group_n);
+    c.n0 = (g * a.group_n + r % gn) * a.tile_n;
+    c.m0 = r / gn;
+  } else {
+    c.n0 = (mn % a.num_n_tiles) * a.tile_n;
+    c.m0 = (mn / a.num_n_tiles);
+  }
   c.kb0 = c.split * a.kb_per_split;
   c.kb1 = min(KB, c.kb0 + a.kb_per_split);
   return c;

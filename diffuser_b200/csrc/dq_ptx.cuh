@@ -327,6 +327,22 @@ __device__ __forceinline__ void tc_mma_ts_pair_elect(uint32_t d_tmem, uint32_t a
       : "memory");
 }
 
+// Pair MMA with both operands in shared memory (A: 128 rows per CTA, B: the
+// CTA's half of the N columns), M = 256, kind::f16; elected-lane issue.
+__device__ __forceinline__ void tc_mma_ss_pair_elect(uint32_t d_tmem, uint64_t a_desc,
+                                                     uint64_t b_desc, uint32_t idesc,
+                                                     uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8, %9, %10, %11, "
+      "%12}, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u),
+      "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      : "memory");
+}
+
 __device__ __forceinline__ void tc_commit_pair_elect(uint32_t bar) {
   asm volatile(
       "{\n\t.reg .pred e;\n\t"

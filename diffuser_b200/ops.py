@@ -219,7 +219,8 @@ def device_error(device=None) -> int:
 
 
 def set_pair_mode(mode: int = 0) -> None:
-    """0 = automatic, 1 = one CTA per 128-row tile, 2 = CTA pairs (256-row tiles)."""
+    """0 = automatic, 1 = fused one-CTA tiles, 2 = fused CTA-pair tiles,
+    3 = two-phase (dequantize into bf16 scratch, then the bf16 pair GEMM)."""
     _lib.check("dq_set_pair_mode", _lib.lib().dq_set_pair_mode(int(mode)))
 
 
@@ -234,5 +235,7 @@ def plan_info(M: int, N: int, K: int, fmt: int = _lib.DQ_FMT_NF4) -> dict:
     _lib.check("dq_plan_info", _lib.lib().dq_plan_info(int(M), int(N), int(K), int(fmt),
                                                        *[ctypes.byref(v) for v in vals]))
     pair, bm, splits, grid = (v.value for v in vals)
-    return {"kernel": "dq_gemm2_kernel (CTA pair)" if pair else "dq_gemm_kernel (one CTA)",
-            "pair": bool(pair), "bm": bm, "splits": splits, "grid": grid}
+    kernel = {0: "dq_gemm_kernel (one CTA)", 1: "dq_gemm2_kernel (CTA pair)",
+              2: "bf16_gemm2_kernel (CTA pair) after dequant"}[pair]
+    return {"kernel": kernel, "pair": pair >= 1, "twophase": pair == 2, "bm": bm, "splits": splits,
+            "grid": grid}

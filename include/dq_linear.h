@@ -82,8 +82,9 @@ int dq_dequant_fp8(const uint8_t* w8, float scale, int64_t n_elems,
                    void* out_bf16, dq_stream_t stream);
 
 /* ------------------------------------------------------------------ linear
- * Bytes of caller-provided scratch the linear needs for this shape (split-K
- * partial sums; 0 when the shape runs unsplit). */
+ * Bytes of caller-provided scratch the linear needs for this shape: split-K
+ * partial sums for small token counts, the bf16 weight (N*K*2) for the
+ * two-phase plan of large ones, else 0. */
 size_t dq_workspace_size(int64_t M, int64_t N, int64_t K, int fmt);
 
 /* y = x . dequant(W)^T + bias, dequantization fused into a tcgen05 GEMM.
@@ -129,8 +130,10 @@ int dq_device_error(int* code, dq_stream_t stream);
  * (16..256, multiple of 16; 0 = automatic) and split-K count (0 = auto). */
 int dq_set_tile_override(int bm, int splits);
 
-/* Kernel-family override for benchmarking: 0 = automatic, 1 = one CTA per
- * tile (128 weight rows), 2 = CTA-pair tiles (256 weight rows, x-tile >= 64). */
+/* Kernel-family override for benchmarking: 0 = automatic, 1 = fused, one CTA
+ * per tile (128 weight rows), 2 = fused, CTA-pair tiles (256 weight rows,
+ * x-tile >= 64), 3 = two-phase: dequantize the weight once into bf16 scratch
+ * (part of the workspace), then a bf16 CTA-pair GEMM (automatic for M >= 1024). */
 int dq_set_pair_mode(int mode);
 
 /* ------------------------------------------------- column-parallel linear
@@ -171,9 +174,10 @@ int dq_tp_linear_fp8(const void* x, int64_t M, int64_t K, const uint8_t* w8_shar
                      dq_stream_t stream);
 
 /* Describes the launch plan dq_linear_* uses for this shape on the current
- * device: *pair = 1 for CTA-pair tiles (256 weight rows per tile) or 0 for
- * one-CTA tiles (128 rows), *bm = x-tile rows, *splits = split-K count,
- * *grid = CTAs launched.  A diagnostic query with no reference counterpart. */
+ * device: *pair = 0 for fused one-CTA tiles (128 weight rows), 1 for fused
+ * CTA-pair tiles (256 rows), 2 for the two-phase plan (dequantize, then the
+ * bf16 pair GEMM); *bm = x-tile rows, *splits = split-K count, *grid = CTAs
+ * launched.  A diagnostic query with no reference counterpart. */
 int dq_plan_info(int64_t M, int64_t N, int64_t K, int fmt, int* pair, int* bm, int* splits,
                  int* grid);
 

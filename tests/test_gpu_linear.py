@@ -86,6 +86,24 @@ def test_every_tile_height(ops, fmt, bm):
 
 @pytest.mark.parametrize("fmt", ["nf4", "fp8"])
 @pytest.mark.parametrize("bm", [64, 128, 192, 256])
+@pytest.mark.parametrize("m,n,k", [(300, 640, 512), (1000, 136, 1088), (70, 264, 3072)])
+def test_two_phase(ops, fmt, bm, m, n, k):
+    # dequantize once into bf16 scratch, then the bf16 CTA-pair GEMM
+    x, w, bias, ref = _case(m, n, k, 3 * bm + n, fmt, with_bias=True)
+    ops.set_pair_mode(3)
+    ops.set_tile_override(bm, 0)
+    try:
+        assert ops.plan_info(m, n, k, 0 if fmt == "nf4" else 1)["twophase"]
+        y = _run(ops, fmt, x, w, bias, n)
+        torch.cuda.synchronize()
+    finally:
+        ops.set_tile_override(0, 0)
+        ops.set_pair_mode(0)
+    assert R.rel_err(to_bits(y), ref) <= TOL
+
+
+@pytest.mark.parametrize("fmt", ["nf4", "fp8"])
+@pytest.mark.parametrize("bm", [64, 128, 192, 256])
 @pytest.mark.parametrize("m,n,k", [(300, 640, 512), (1000, 136, 1088)])
 def test_cta_pair_tiles(ops, fmt, bm, m, n, k):
     # two-SM kernel: 256 weight rows per CTA pair, bm tokens split across the pair
@@ -172,7 +190,8 @@ def test_full_size_fp8(ops):
 
 
 @pytest.mark.parametrize("fmt", ["nf4", "fp8"])
-@pytest.mark.parametrize("mode,bm", [(1, 128), (1, 192), (1, 256), (2, 192), (2, 256)])
+@pytest.mark.parametrize("mode,bm", [(1, 128), (1, 192), (1, 256), (2, 192), (2, 256),
+                                     (3, 128), (3, 256)])
 def test_full_size_every_plan(ops, fmt, mode, bm):
     # every tile plan at the benchmarked shape, twice: a pipeline race shows
     # up as a large or run-to-run varying error here
@@ -200,9 +219,13 @@ def test_golden_linear(ops):
 
 
 def test_plan_choice(ops):
-    # large token batches take CTA-pair tiles, decode-sized batches one-CTA tiles
+    # large token batches dequantize once and run the bf16 pair GEMM,
+    # mid-sized ones the fused kernels, decode-sized ones one-CTA tiles
     big = ops.plan_info(4608, 12288, 3072)
-    assert big["pair"] and big["bm"] == 256 and big["splits"] == 1
+    assert big["twophase"] and big["bm"] == 256 and big["splits"] == 1
+    assert ops.workspace_size(4608, 12288, 3072) == 12288 * 3072 * 2
+    mid = ops.plan_info(512, 12288, 3072)
+    assert not mid["twophase"]
     small = ops.plan_info(16, 3072, 3072)
     assert not small["pair"] and small["bm"] == 16 and small["splits"] > 1
 
