@@ -13,9 +13,11 @@
 #include <mutex>
 
 #include "../../include/dq_linear.h"
+#include "../../include/dq_dit.h"
 #include "dq_gemm.cuh"
 #include "dq_gemm2.cuh"
 #include "dq_bf16gemm2.cuh"
+#include "dq_dit.cuh"
 
 #define DQ_VERSION_STRING "dqlinear-b200 0.1.0 (sm_100a)"
 
@@ -945,6 +947,74 @@ int dq_tp_linear_fp8(const void* x, int64_t M, int64_t K, const uint8_t* w8_shar
                      dq_stream_t stream) {
   return tp_impl(kFmtFP8, x, M, K, w8_shard, nullptr, scale, bias_shard, N, rank, world, y_ranks,
                  flag_ranks, counter, epoch, static_cast<cudaStream_t>(stream));
+}
+
+int dq_qk_norm_rope(const void* img, int64_t ld_img, const void* txt, int64_t ld_txt, int B,
+                    int S_img, int S_txt, int H, int D, const void* w_img, const void* w_txt,
+                    const float* cos_t, const float* sin_t, float eps, void* out,
+                    dq_stream_t stream) {
+  if (B <= 0 || S_img < 0 || S_txt < 0 || H <= 0 || D <= 0 || D % 64 != 0 || D > 256)
+    return DQ_ERR_SHAPE;
+  if (img == nullptr || out == nullptr || (S_txt > 0 && txt == nullptr)) return DQ_ERR_ARG;
+  if ((cos_t == nullptr) != (sin_t == nullptr)) return DQ_ERR_ARG;
+  // with text tokens both streams are normalized or neither
+  if (S_txt > 0 && (w_img == nullptr) != (w_txt == nullptr)) return DQ_ERR_ARG;
+  if (ld_img < static_cast<int64_t>(H) * D || (S_txt > 0 && ld_txt < static_cast<int64_t>(H) * D))
+    return DQ_ERR_SHAPE;
+  const int64_t warps = static_cast<int64_t>(B) * (S_img + S_txt) * H;
+  if (warps == 0) return DQ_OK;
+  const int64_t blocks = (warps * 32 + 255) / 256;
+  if (blocks > INT32_MAX) return DQ_ERR_SHAPE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto bf = [](const void* p) { return static_cast<const __nv_bfloat16*>(p); };
+  switch (D / 32) {
+    case 2:
+      qk_norm_rope_kernel<2><<<static_cast<int>(blocks), 256, 0, st>>>(
+          bf(img), ld_img, bf(txt), ld_txt, B, S_img, S_txt, H, bf(w_img), bf(w_txt), cos_t, sin_t,
+          eps, static_cast<__nv_bfloat16*>(out));
+      break;
+    case 4:
+      qk_norm_rope_kernel<4><<<static_cast<int>(blocks), 256, 0, st>>>(
+          bf(img), ld_img, bf(txt), ld_txt, B, S_img, S_txt, H, bf(w_img), bf(w_txt), cos_t, sin_t,
+          eps, static_cast<__nv_bfloat16*>(out));
+      break;
+    case 6:
+      qk_norm_rope_kernel<6><<<static_cast<int>(blocks), 256, 0, st>>>(
+          bf(img), ld_img, bf(txt), ld_txt, B, S_img, S_txt, H, bf(w_img), bf(w_txt), cos_t, sin_t,
+          eps, static_cast<__nv_bfloat16*>(out));
+      break;
+    case 8:
+      qk_norm_rope_kernel<8><<<static_cast<int>(blocks), 256, 0, st>>>(
+          bf(img), ld_img, bf(txt), ld_txt, B, S_img, S_txt, H, bf(w_img), bf(w_txt), cos_t, sin_t,
+          eps, static_cast<__nv_bfloat16*>(out));
+      break;
+    default:
+      return DQ_ERR_SHAPE;
+  }
+  return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
+}
+
+int dq_heads_to_tokens(const void* in, int B, int H, int S_txt, int S_img, int D, void* out_txt,
+                       void* out_img, dq_stream_t stream) {
+  if (B <= 0 || H <= 0 || S_txt < 0 || S_img < 0 || D <= 0 || D % 64 != 0 || D > 256)
+    return DQ_ERR_SHAPE;
+  if (in == nullptr || out_img == nullptr || (S_txt > 0 && out_txt == nullptr)) return DQ_ERR_ARG;
+  const int64_t warps = static_cast<int64_t>(B) * (S_img + S_txt) * H;
+  if (warps == 0) return DQ_OK;
+  const int64_t blocks = (warps * 32 + 255) / 256;
+  if (blocks > INT32_MAX) return DQ_ERR_SHAPE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(in);
+  __nv_bfloat16* ot = static_cast<__nv_bfloat16*>(out_txt);
+  __nv_bfloat16* oi = static_cast<__nv_bfloat16*>(out_img);
+  switch (D / 32) {
+    case 2: heads_to_tokens_kernel<2><<<static_cast<int>(blocks), 256, 0, st>>>(src, B, H, S_txt, S_img, ot, oi); break;
+    case 4: heads_to_tokens_kernel<4><<<static_cast<int>(blocks), 256, 0, st>>>(src, B, H, S_txt, S_img, ot, oi); break;
+    case 6: heads_to_tokens_kernel<6><<<static_cast<int>(blocks), 256, 0, st>>>(src, B, H, S_txt, S_img, ot, oi); break;
+    case 8: heads_to_tokens_kernel<8><<<static_cast<int>(blocks), 256, 0, st>>>(src, B, H, S_txt, S_img, ot, oi); break;
+    default: return DQ_ERR_SHAPE;
+  }
+  return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
 }
 
 int dq_device_error(int* code, dq_stream_t stream) {

@@ -11,13 +11,61 @@ cast-set linears (R/checkpoint_flux.R:21-42) become fused NF4 linears through
 """
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
 import torch.nn.functional as F
 from torch import nn
 
-from . import modules
+from . import _lib, modules
+
+
+# ------------------------------------------------------ fused attention glue
+def _fused_ok(x, dim_head: int) -> bool:
+    """The CUDA prologue / epilogue kernels serve bf16 CUDA tensors with a head
+    dimension that is a multiple of 64 (FLUX: 128); other cases (the float32
+    CPU fixture model) take the tensor-op path."""
+    return x.is_cuda and x.dtype == torch.bfloat16 and dim_head % 64 == 0 and dim_head <= 256
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def qk_norm_rope(img, txt, heads: int, w_img=None, w_txt=None, rope=None, eps: float = 1e-6):
+    """Per-head RMS norm + [text; image] concatenation + transpose + rotary
+    embedding in one kernel: img [B, S_img, H*D] (and txt [B, S_txt, H*D]) ->
+    [B, H, S_txt + S_img, D] bf16."""
+    b, s_img, hd = img.shape
+    d = hd // heads
+    s_txt = 0 if txt is None else txt.shape[1]
+    img = img if img.stride(-1) == 1 else img.contiguous()
+    if txt is not None and txt.stride(-1) != 1:
+        txt = txt.contiguous()
+    out = torch.empty((b, heads, s_txt + s_img, d), dtype=torch.bfloat16, device=img.device)
+    cos = sin = None
+    if rope is not None:
+        cos, sin = rope[0].contiguous(), rope[1].contiguous()
+    stream = ctypes.c_void_p(torch.cuda.current_stream(img.device).cuda_stream)
+    rc = _lib.lib().dq_qk_norm_rope(
+        _ptr(img), img.stride(1), _ptr(txt), 0 if txt is None else txt.stride(1), b, s_img, s_txt,
+        heads, d, _ptr(w_img), _ptr(w_txt), _ptr(cos), _ptr(sin), ctypes.c_float(eps), _ptr(out), stream)
+    _lib.check("dq_qk_norm_rope", rc)
+    return out
+
+
+def heads_to_tokens(x, s_txt: int):
+    """[B, H, S_txt + S_img, D] -> (txt [B, S_txt, H*D] or None, img [B, S_img, H*D])."""
+    b, h, s, d = x.shape
+    x = x if x.is_contiguous() else x.contiguous()
+    s_img = s - s_txt
+    img = torch.empty((b, s_img, h * d), dtype=torch.bfloat16, device=x.device)
+    txt = torch.empty((b, s_txt, h * d), dtype=torch.bfloat16, device=x.device) if s_txt else None
+    stream = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
+    rc = _lib.lib().dq_heads_to_tokens(_ptr(x), b, h, s_txt, s_img, d, _ptr(txt), _ptr(img), stream)
+    _lib.check("dq_heads_to_tokens", rc)
+    return txt, img
 
 
 # --------------------------------------------------------------- primitives
@@ -200,6 +248,8 @@ class FluxAttention(nn.Module):
 
     def forward(self, x, ctx=None, rope=None):
         h = self.heads
+        if _fused_ok(x, self.norm_q.weight.shape[0]):
+            return self._forward_fused(x, ctx, rope)
         q = self.norm_q(self.to_q(x).unflatten(-1, (h, -1)))
         k = self.norm_k(self.to_k(x).unflatten(-1, (h, -1)))
         v = self.to_v(x).unflatten(-1, (h, -1))
@@ -225,6 +275,27 @@ class FluxAttention(nn.Module):
         if self.pre_only:
             return out
         return self.to_out[0](out)
+
+    def _forward_fused(self, x, ctx, rope):
+        """The same computation with the norm / concat / transpose / rotary
+        chain in one kernel per tensor and the split back in one more."""
+        h = self.heads
+        q_t = k_t = v_t = None
+        wq_t = wk_t = None
+        if ctx is not None:
+            q_t, k_t, v_t = self.add_q_proj(ctx), self.add_k_proj(ctx), self.add_v_proj(ctx)
+            wq_t, wk_t = self.norm_added_q.weight, self.norm_added_k.weight
+        q = qk_norm_rope(self.to_q(x), q_t, h, self.norm_q.weight, wq_t, rope, self.norm_q.eps)
+        k = qk_norm_rope(self.to_k(x), k_t, h, self.norm_k.weight, wk_t, rope, self.norm_k.eps)
+        v = qk_norm_rope(self.to_v(x), v_t, h)
+        out = F.scaled_dot_product_attention(q, k, v, dropout_p=0.0, is_causal=False)
+        txt_len = 0 if ctx is None else ctx.shape[1]
+        txt, img = heads_to_tokens(out, txt_len)
+        if ctx is not None:
+            return self.to_out[0](img), self.to_add_out(txt)
+        if self.pre_only:
+            return img
+        return self.to_out[0](img)
 
 
 class DoubleBlock(nn.Module):

@@ -1,0 +1,39 @@
+/* dq_dit.h -- fused attention prologue / epilogue for the FLUX DiT blocks
+ * that call the quantized linears (same library as dq_linear.h).
+ *
+ * These have no single reference counterpart: each replaces a chain of the
+ * reference's tensor ops around the attention (R/dit_flux_modules.R:161-212:
+ * per-head ltx23_rms_norm, the [text; image] concatenation, the transpose to
+ * head-major, flux_apply_rotary_emb R/rope_flux.R:96-110, and the way back).
+ * bf16 tensors, device pointers, the given stream; D (the head dimension) a
+ * multiple of 64 up to 256. */
+#ifndef DQ_DIT_H
+#define DQ_DIT_H
+
+#include <stdint.h>
+#include "dq_linear.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* img [B, S_img, H*D] (row stride ld_img elements) and, if txt != NULL, txt
+ * [B, S_txt, H*D] (row stride ld_txt) -> out [B, H, S_txt + S_img, D], text
+ * first.  w_img / w_txt: RMS-norm weights [D] (NULL: no norm; eps as the
+ * module's); cos_t / sin_t: float32 rotary tables [S_txt + S_img, D] (NULL: no
+ * rotation). */
+int dq_qk_norm_rope(const void* img, int64_t ld_img, const void* txt, int64_t ld_txt, int B,
+                    int S_img, int S_txt, int H, int D, const void* w_img, const void* w_txt,
+                    const float* cos_t, const float* sin_t, float eps, void* out,
+                    dq_stream_t stream);
+
+/* in [B, H, S_txt + S_img, D] -> out_txt [B, S_txt, H*D] (if S_txt > 0) and
+ * out_img [B, S_img, H*D]. */
+int dq_heads_to_tokens(const void* in, int B, int H, int S_txt, int S_img, int D, void* out_txt,
+                       void* out_img, dq_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DQ_DIT_H */

@@ -10,14 +10,17 @@ import pytest
 from diffuser_b200 import _lib
 from diffuser_b200 import build as B
 
-HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
-                      "include", "dq_linear.h")
+INCLUDE = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
+HEADER = os.path.join(INCLUDE, "dq_linear.h")
 
 
 def _header_functions():
-    src = open(HEADER).read()
-    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-    return sorted(set(re.findall(r"\b(dq_[a-z0-9_]+)\s*\(", src)))
+    names = set()
+    for h in sorted(os.listdir(INCLUDE)):
+        if h.endswith(".h"):
+            src = re.sub(r"/\*.*?\*/", "", open(os.path.join(INCLUDE, h)).read(), flags=re.S)
+            names.update(re.findall(r"\b(dq_[a-z0-9_]+)\s*\(", src))
+    return sorted(names)
 
 
 @pytest.fixture(scope="module")

@@ -66,3 +66,66 @@ def test_flux_dit_fused_matches_reference_backend():
     assert torch.isfinite(out.float()).all()
     cos = torch.nn.functional.cosine_similarity(out.float().flatten(), ref.float().flatten(), dim=0)
     assert cos.item() >= 0.999, cos.item()
+
+
+def test_flux_step_captures_in_a_cuda_graph():
+    # the engine's launches (ctypes on the current stream, cluster launches,
+    # cached workspaces) capture; replay reproduces the eager step bit for bit
+    from diffuser_b200 import flux, ops
+    dev = torch.device("cuda", 0)
+    model = flux.build_flux_nf4(dev, seed=1, num_layers=2, num_single_layers=2)
+    x, text, pooled, rope = _inputs(dev)
+    t = torch.ones(1, dtype=torch.float32, device=dev)
+
+    def step():
+        with torch.no_grad():
+            return flux.euler_step(model(x, text, pooled, t, rope), 1.0, 0.75, x)
+
+    eager = step()
+    step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = step()
+    g.replay()
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    assert torch.equal(out, eager)
+
+
+def test_fused_attention_glue_matches_tensor_ops():
+    # one kernel for norm + [text; image] + transpose + rotary vs the tensor-op
+    # chain of the harness (R/dit_flux_modules.R:161-190, R/rope_flux.R:96-110)
+    from diffuser_b200 import flux
+    torch.manual_seed(0)
+    dev = torch.device("cuda", 0)
+    for (B, S_img, S_txt, H, D) in ((2, 37, 9, 3, 128), (1, 64, 0, 2, 64), (1, 5, 3, 2, 256)):
+        img = torch.randn(B, S_img, H * D, device=dev).to(torch.bfloat16)
+        txt = torch.randn(B, S_txt, H * D, device=dev).to(torch.bfloat16) if S_txt else None
+        w_img = (1 + 0.1 * torch.randn(D, device=dev)).to(torch.bfloat16)
+        w_txt = (1 + 0.1 * torch.randn(D, device=dev)).to(torch.bfloat16)
+        pos = torch.randint(0, 64, (S_txt + S_img, 3), device=dev).float()
+        axes = {64: (16, 24, 24), 128: (16, 56, 56), 256: (32, 112, 112)}[D]
+        rope = flux.pos_embed(pos, axes)
+        norm_i, norm_t = flux.RMSNorm(D).to(dev, torch.bfloat16), flux.RMSNorm(D).to(dev, torch.bfloat16)
+        with torch.no_grad():
+            norm_i.weight.copy_(w_img)
+            norm_t.weight.copy_(w_txt)
+            parts = [norm_i(img.unflatten(-1, (H, -1)))]
+            if S_txt:
+                parts.insert(0, norm_t(txt.unflatten(-1, (H, -1))))
+            ref = flux.apply_rotary_emb(torch.cat(parts, dim=1).transpose(1, 2), rope)
+            got = flux.qk_norm_rope(img, txt, H, w_img, w_txt if S_txt else None, rope)
+            # the mean is summed in another order: at most one bf16 step apart
+            step = ref.float().abs().clamp(min=1e-30) * 2.0 ** -7
+            assert ((got.float() - ref.float()).abs() <= step + 1e-30).all()
+            assert (got != ref).float().mean().item() < 0.02
+            vparts = [img.unflatten(-1, (H, -1))]
+            if S_txt:
+                vparts.insert(0, txt.unflatten(-1, (H, -1)))
+            vref = torch.cat(vparts, dim=1).transpose(1, 2)
+            assert torch.equal(flux.qk_norm_rope(img, txt, H), vref)
+            t_out, i_out = flux.heads_to_tokens(vref.contiguous(), S_txt)
+            assert torch.equal(i_out, img)
+            if S_txt:
+                assert torch.equal(t_out, txt)
