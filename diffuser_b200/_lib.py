@@ -53,6 +53,12 @@ SIGNATURES = {
     "dq_heads_to_tokens": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                           ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
                                           ctypes.c_void_p]),
+    "dq_linear_nf4_ex": (ctypes.c_int, [ctypes.c_void_p, _c_i64, _c_i64, ctypes.c_void_p, ctypes.c_void_p,
+                                        ctypes.c_void_p, _c_i64, ctypes.c_int, ctypes.c_void_p,
+                                        ctypes.c_void_p, _c_sz, ctypes.c_void_p]),
+    "dq_linear_fp8_ex": (ctypes.c_int, [ctypes.c_void_p, _c_i64, _c_i64, ctypes.c_void_p, ctypes.c_float,
+                                        ctypes.c_void_p, _c_i64, ctypes.c_int, ctypes.c_void_p,
+                                        ctypes.c_void_p, _c_sz, ctypes.c_void_p]),
     "dq_plan_info": (ctypes.c_int, [_c_i64, _c_i64, _c_i64, ctypes.c_int] + [ctypes.POINTER(ctypes.c_int)] * 4),
 }
 
@@ -61,6 +67,7 @@ DQ_ERR_TIMEOUT = 5
 DQ_ERR_SCRATCH_LIMIT = 9
 DQ_NOALLOC_SCRATCH_BYTES = 8 << 20
 DQ_IPC_HANDLE_BYTES = 64
+DQ_ACT_NONE, DQ_ACT_GELU_TANH = 0, 1
 DQ_FMT_NF4, DQ_FMT_FP8 = 0, 1
 DQ_DTYPE_F32, DQ_DTYPE_BF16 = 0, 1
 

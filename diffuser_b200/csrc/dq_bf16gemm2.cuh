@@ -9,8 +9,23 @@
 // no weight in tensor memory both 256-column accumulators fit, so the epilogue
 // of one tile overlaps the MMAs of the next.
 //
-// Warps: 0-3 epilogue, 4 producer (TMA of the A and X halves of each stage),
-// 5 MMA (leader CTA; elected lane issues).  Cross-CTA protocol as in
+// Warps: 0-7 epilogue (two per TMEM lane quadrant, each draining half of the
+// tile's columns), 8 producer (TMA of the A and X halves of each stage), 9 MMA
+// (leader CTA; elected lane issues).  Eight epilogue warps keep the drain of
+// one tile shorter than the next tile's MMAs even with an activation in the
+// epilogue; with four, a GELU-tanh epilogue outlasted them.
+//
+// With FMT >= 0 (kFmtNF4 / kFmtFP8) the launch also dequantizes the weight:
+// four more warps per CTA decode the packed weight into the bf16 scratch
+// (the arithmetic of dequant_nf4_kernel / dequant_fp8_kernel, bit-exact with
+// the reference's dequantization) one weight group of the grouped tile order
+// at a time, every warp counting itself done on dq_ready[g]; the producer
+// waits (bounded) for a group's count before its first TMA load of that
+// group.  The decode then runs under the MMAs of the earlier groups instead
+// of before the GEMM; the first group is made narrow so the first MMAs start
+// after a short decode.  The dequantizing warps wait on nothing.
+//
+// Cross-CTA protocol as in
 // dq_gemm2.cuh: both CTAs' TMA loads complete on the leader's full barrier,
 // the leader's commits multicast stage-empty and accumulator-full to both
 // CTAs, both CTAs' epilogue warps arrive on the leader's accumulator-empty
@@ -21,7 +36,7 @@
 
 namespace dq {
 
-template <int BM>
+template <int BM, int FMT = -1>
 struct Bf16PairCfg {
   static_assert(BM % 32 == 0 && BM >= 64 && BM <= 256, "pair tiles need BM in {64..256}, /32");
   static constexpr int kHalfBM = BM / 2;
@@ -29,16 +44,20 @@ struct Bf16PairCfg {
   static constexpr int kAccStride = BM;
   static constexpr int kAStageBytes = 128 * 128;  // 128 weight rows x 64 bf16, SW128 K-major
   static constexpr int kXStageBytes = kHalfBM * 128;
+  static constexpr int kEpiWarps = 8;
   static constexpr int kEpiCols = 32;
-  static constexpr int kEpiBytes = 4 * kEpiCols * 32 * 4;
+  static constexpr int kEpiBytes = kEpiWarps * kEpiCols * 32 * 4;
   static constexpr int kSmemLimit = 227 * 1024;
   static constexpr int kStagesFit =
       (kSmemLimit - kEpiBytes - 2048 - 1024) / (kAStageBytes + kXStageBytes);
   static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
   static_assert(kStages >= 3, "need three stages in flight");
-  static constexpr int kProducerWarp = 4;
-  static constexpr int kMmaWarp = 5;
-  static constexpr int kThreads = 6 * 32;
+  static constexpr int kProducerWarp = kEpiWarps;
+  static constexpr int kMmaWarp = kEpiWarps + 1;
+  static constexpr int kDqWarp0 = kEpiWarps + 2;
+  static constexpr int kDqWarps = FMT >= 0 ? 4 : 0;
+  static constexpr int kThreads = (kEpiWarps + 2 + kDqWarps) * 32;
+  static_assert(BM % (2 * kEpiCols) == 0, "each epilogue warp drains whole 32-column chunks");
   static constexpr int kNumBars = 2 * kStages + 2 * kNumAcc + 1;
   static constexpr int kOffA = 0;
   static constexpr int kOffX = kStages * kAStageBytes;
@@ -53,11 +72,80 @@ struct Bf16PairCfg {
   static constexpr uint32_t kTxBytes = 2 * (kAStageBytes + kXStageBytes);  // both CTAs
 };
 
-template <int BM>
-__global__ void __launch_bounds__(Bf16PairCfg<BM>::kThreads, 1)
+// Decode weight rows [r0, r1) of the flat packed weight into dq_out: the
+// calling thread's share (thread tid of nthr) of the 16-byte chunks, four
+// chunks in flight per thread.
+template <int FMT>
+__device__ __forceinline__ void dequant_rows(const GemmArgs& a, int64_t r0, int64_t r1, int tid,
+                                             int nthr) {
+  const int64_t K = a.K;
+  if constexpr (FMT == kFmtNF4) {
+    // 32 weights per chunk; block scale c >> 1
+    const uint4* src = reinterpret_cast<const uint4*>(a.dq_w);
+    uint4* dst = reinterpret_cast<uint4*>(a.dq_out);
+    const int64_t c1 = r1 * K / 32;
+    for (int64_t c = r0 * K / 32 + tid; c < c1; c += 4ll * nthr) {
+      uint4 p[4];
+      float am[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t cu = c + static_cast<int64_t>(u) * nthr;
+        if (cu < c1) {
+          p[u] = __ldg(src + cu);
+          am[u] = __ldg(a.absmax + (cu >> 1));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t cu = c + static_cast<int64_t>(u) * nthr;
+        if (cu < c1) {
+          const Nf4Planes planes = nf4_scaled_planes(nf4_scale2(am[u]));
+          uint32_t o[16];
+          nf4_decode_word(p[u].x, planes, o + 0);
+          nf4_decode_word(p[u].y, planes, o + 4);
+          nf4_decode_word(p[u].z, planes, o + 8);
+          nf4_decode_word(p[u].w, planes, o + 12);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            dst[4 * cu + j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+        }
+      }
+    }
+  } else {
+    // 16 weights per chunk (K % 16 == 0, so rows hold whole chunks)
+    const float s = __bfloat162float(__float2bfloat16_rn(a.fp8_scale));
+    const uint4* src = reinterpret_cast<const uint4*>(a.dq_w);
+    uint4* dst = reinterpret_cast<uint4*>(a.dq_out);
+    const int64_t c1 = r1 * K / 16;
+    for (int64_t c = r0 * K / 16 + tid; c < c1; c += 4ll * nthr) {
+      uint4 p[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t cu = c + static_cast<int64_t>(u) * nthr;
+        if (cu < c1) p[u] = __ldg(src + cu);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t cu = c + static_cast<int64_t>(u) * nthr;
+        if (cu < c1) {
+          uint32_t o[8];
+          fp8_decode_word(p[u].x, s, o + 0);
+          fp8_decode_word(p[u].y, s, o + 2);
+          fp8_decode_word(p[u].z, s, o + 4);
+          fp8_decode_word(p[u].w, s, o + 6);
+          dst[2 * cu] = make_uint4(o[0], o[1], o[2], o[3]);
+          dst[2 * cu + 1] = make_uint4(o[4], o[5], o[6], o[7]);
+        }
+      }
+    }
+  }
+}
+
+template <int BM, int FMT = -1>
+__global__ void __launch_bounds__(Bf16PairCfg<BM, FMT>::kThreads, 1)
     bf16_gemm2_kernel(const __grid_constant__ CUtensorMap tmap_x,
                       const __grid_constant__ CUtensorMap tmap_a, const GemmArgs args) {
-  using C = Bf16PairCfg<BM>;
+  using C = Bf16PairCfg<BM, FMT>;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -87,7 +175,7 @@ __global__ void __launch_bounds__(Bf16PairCfg<BM>::kThreads, 1)
     }
     for (int a = 0; a < C::kNumAcc; ++a) {
       mbar_init(accfull_bar(a), 1);
-      mbar_init(accempty_bar(a), 2 * 4);  // 4 epilogue warps x 2 CTAs
+      mbar_init(accempty_bar(a), 2 * C::kEpiWarps);  // every epilogue warp of both CTAs
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -110,8 +198,17 @@ __global__ void __launch_bounds__(Bf16PairCfg<BM>::kThreads, 1)
     if (lane == 0) {
       int it = 0;
       bool ok = true;
+      int ready_group = -1;  // weight groups up to this one are decoded
       for (int t = pair; t < args.num_tiles && ok; t += npairs) {
         const TileCoord tc = tile_coord(args, t, KB);
+        if constexpr (FMT >= 0) {
+          if (tc.group > ready_group) {
+            const unsigned int target = gridDim.x * C::kDqWarps;
+            if (!wait_count_geq(args.dq_ready + tc.group, target, abort_flag)) break;
+            fence_proxy_async_global();
+            ready_group = tc.group;
+          }
+        }
         const int m_half = tc.m0 * BM + static_cast<int>(rank) * C::kHalfBM;
         const int n_row = tc.n0 + 128 * static_cast<int>(rank);
         for (int kb = tc.kb0; kb < tc.kb1; ++kb, ++it) {
@@ -181,13 +278,34 @@ __global__ void __launch_bounds__(Bf16PairCfg<BM>::kThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp < 4) {
+  } else if (FMT >= 0 && warp >= C::kDqWarp0) {
+    // ------------------------------------------------------ weight decode
+    if constexpr (FMT >= 0) {
+      const int nthr = static_cast<int>(gridDim.x) * C::kDqWarps * 32;
+      const int tid = static_cast<int>(blockIdx.x) * C::kDqWarps * 32 + threadIdx.x - C::kDqWarp0 * 32;
+      const int g0 = first_group_width(args.group_n, args.group0_n, args.num_n_tiles);
+      int nb = 0;
+      for (int g = 0; nb < args.num_n_tiles; ++g) {
+        const int gn = g == 0 ? g0 : min(args.group_n, args.num_n_tiles - nb);
+        const int64_t r0 = static_cast<int64_t>(nb) * 256;
+        const int64_t r1 = min(static_cast<int64_t>(args.N), static_cast<int64_t>(nb + gn) * 256);
+        dequant_rows<FMT>(args, r0, r1, tid, nthr);
+        // every lane's stores, then the warp's count (release)
+        fence_proxy_async_global();
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(args.dq_ready + g, 1u);
+        nb += gn;
+      }
+    }
+  } else if (warp < C::kEpiWarps) {
     // ------------------------------------------------------------ epilogue
     constexpr int EC = C::kEpiCols;
-    const int quad = warp;
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int half = warp >> 2;  // which half of the tile's columns it drains
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
-    uint8_t* stg = smem + C::kOffEpi + quad * (EC * 32 * 4);
-    const uint32_t stg_s = sbase + C::kOffEpi + quad * (EC * 32 * 4);
+    uint8_t* stg = smem + C::kOffEpi + warp * (EC * 32 * 4);
+    const uint32_t stg_s = sbase + C::kOffEpi + warp * (EC * 32 * 4);
     int acc = 0;
     uint32_t accphase = 0;
     for (int t = pair; t < args.num_tiles; t += npairs) {
@@ -202,14 +320,15 @@ __global__ void __launch_bounds__(Bf16PairCfg<BM>::kThreads, 1)
       const uint32_t d_addr = tmem_base + lane_addr + static_cast<uint32_t>(acc * C::kAccStride);
       const uint32_t lead_accempty = mapa_shared(accempty_bar(acc), 0);
       const int ncol0 = nbase + quad * 32;
-      constexpr int NC = BM / EC;
+      constexpr int NC = BM / EC / 2;  // chunks per warp
+      const int c0 = half * NC;
       uint32_t v[2][32];
-      tmem_ld_x32(d_addr, v[0]);
+      tmem_ld_x32(d_addr + 32u * c0, v[0]);
 #pragma unroll
       for (int c = 0; c < NC; ++c) {
         tmem_wait_ld();
         if (c + 1 < NC) {
-          tmem_ld_x32(d_addr + 32u * (c + 1), v[(c + 1) & 1]);
+          tmem_ld_x32(d_addr + 32u * (c0 + c + 1), v[(c + 1) & 1]);
         } else {
           // the whole accumulator has been read: hand it back to the MMA warp
           tc_fence_before();
@@ -217,13 +336,21 @@ __global__ void __launch_bounds__(Bf16PairCfg<BM>::kThreads, 1)
           if (lane == 0) mbar_arrive_cluster(lead_accempty);
         }
         const uint32_t* vc = v[c & 1];
-        const int mrow0 = m0 + EC * c;
+        const int mrow0 = m0 + EC * (c0 + c);
         // stage [EC tokens][32 outputs] bf16, then write 64-byte row segments
         __nv_bfloat16* sb = reinterpret_cast<__nv_bfloat16*>(stg);
+        if (args.act == kActNone) {
 #pragma unroll
-        for (int j = 0; j < EC; ++j)
-          sts16(stg_s + 2u * (j * 32 + lane),
-                __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(vc[j]) + bias)));
+          for (int j = 0; j < EC; ++j)
+            sts16(stg_s + 2u * (j * 32 + lane),
+                  __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(vc[j]) + bias)));
+        } else {
+#pragma unroll
+          for (int j = 0; j < EC; ++j)
+            sts16(stg_s + 2u * (j * 32 + lane),
+                  __bfloat16_as_ushort(__float2bfloat16_rn(
+                      apply_act(__uint_as_float(vc[j]) + bias, args.act))));
+        }
         __syncwarp();
         __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(args.outs[0]);
 #pragma unroll

@@ -153,14 +153,14 @@ __global__ void tp_wait_kernel(const unsigned int* flags, int world, unsigned in
 // Split-K: y = bf16(sum_s partial[s] + bias); four outputs per thread.
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int M, int N,
                                      const __nv_bfloat16* __restrict__ bias,
-                                     __nv_bfloat16* __restrict__ y) {
+                                     __nv_bfloat16* __restrict__ y, int act) {
   const int64_t total = static_cast<int64_t>(M) * N;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total; i += stride) {
     float acc = 0.f;
     for (int s = 0; s < splits; ++s) acc += part[static_cast<size_t>(s) * total + i];
     if (bias != nullptr) acc += __bfloat162float(bias[i % N]);
-    y[i] = __float2bfloat16_rn(acc);
+    y[i] = __float2bfloat16_rn(apply_act(acc, act));
   }
 }
 
@@ -171,8 +171,8 @@ struct DeviceInfo {
   int smem_set[2][2][6] = {};   // [column-parallel][fmt][bm]
   int smem_set2[2][2][6] = {};
   int max_pairs[2][6] = {};     // [fmt][bm]
-  int bf16_smem_set[6] = {};    // bf16 pair GEMM, [bm]
-  int bf16_max_pairs[6] = {};
+  int bf16_smem_set[3][6] = {};    // bf16 pair GEMM, [decoded format + 1][bm]
+  int bf16_max_pairs[3][6] = {};
 };
 
 constexpr int kMaxDevices = 64;
@@ -264,17 +264,30 @@ static constexpr TileShape kShapes[] = {
 // token tile, and the bf16 pair GEMM runs faster than the fused kernels.
 constexpr int64_t kTwoPhaseMinM = 1024;
 
+// Two-phase workspace: the bf16 weight [N, K], then one uint32 counter per
+// weight group (at most one group per 256-row weight tile).
+static size_t twophase_counter_offset(int64_t N, int64_t K) {
+  return (static_cast<size_t>(N) * K * 2 + 255) & ~static_cast<size_t>(255);
+}
+static size_t twophase_counter_bytes(int n_tiles) {
+  return (static_cast<size_t>(n_tiles + 1) * 4 + 255) & ~static_cast<size_t>(255);
+}
+// Weight tiles per group of the two-phase grouped order (16 x 256 rows: a
+// group's bf16 weight stays in L2 while the token tiles sweep past it).
+constexpr int kTwoPhaseGroupN = 16;
+
 static Plan make_plan(int64_t M, int64_t N, int64_t K, int sms, bool allow_split = true,
                       bool allow_twophase = true) {
   Plan p;
   const int KB = static_cast<int>((K + 63) / 64);
-  // 0 automatic, 1 one-CTA fused only, 2 CTA-pair fused only, 3 two-phase only
+  // 0 automatic, 1 one-CTA fused only, 2 CTA-pair fused only, 3 two-phase
+  // only, 4 two-phase only with the dequantization as its own launch
   const int opair = g_override_pair.load();
   const int obm = g_override_bm.load();
   auto units_of = [&](bool pair) { return pair ? sms / 2 : sms; };
   auto n_tiles_of = [&](bool pair) { return static_cast<int>((N + (pair ? 255 : 127)) / (pair ? 256 : 128)); };
   const bool twophase = allow_twophase && M > 64 &&
-                        (opair == 3 || (opair == 0 && M >= kTwoPhaseMinM));
+                        (opair == 3 || opair == 4 || (opair == 0 && M >= kTwoPhaseMinM));
   if (twophase) {
     p.pair = true;
     p.twophase = true;
@@ -338,7 +351,8 @@ static Plan make_plan(int64_t M, int64_t N, int64_t K, int sms, bool allow_split
   p.tiles = base_tiles * p.splits;
   p.grid = std::min(p.tiles, units);  // CTAs (1-CTA kernel) or pairs (pair kernel)
   p.ws = p.splits > 1 ? static_cast<size_t>(p.splits) * M * N * sizeof(float) : 0;
-  if (p.twophase) p.ws = static_cast<size_t>(N) * K * 2;  // the bf16 weight
+  if (p.twophase)  // the bf16 weight, then the weight groups' ready counters
+    p.ws = twophase_counter_offset(N, K) + twophase_counter_bytes(p.n_tiles);
   return p;
 }
 
@@ -424,9 +438,9 @@ static int pair_capacity(DeviceInfo* d, int bm, int* pairs) {
   return rc;
 }
 
-template <int BM>
+template <int BM, int FMT>
 static cudaLaunchConfig_t bf16_pair_config(cudaLaunchAttribute* attr, cudaStream_t st) {
-  using C = Bf16PairCfg<BM>;
+  using C = Bf16PairCfg<BM, FMT>;
   cudaLaunchConfig_t cfg = {};
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
@@ -442,50 +456,73 @@ static cudaLaunchConfig_t bf16_pair_config(cudaLaunchAttribute* attr, cudaStream
 
 // One-time setup of a bf16 pair GEMM instantiation: shared-memory opt-in and
 // the resident-cluster capacity (cached in d->bf16_max_pairs).
-template <int BM>
+template <int BM, int FMT>
 static int bf16_pair_setup(DeviceInfo* d) {
-  using C = Bf16PairCfg<BM>;
+  using C = Bf16PairCfg<BM, FMT>;
   const int bi = bm_index(BM);
-  if (d->bf16_smem_set[bi]) return DQ_OK;
-  auto kern = bf16_gemm2_kernel<BM>;
+  if (d->bf16_smem_set[FMT + 1][bi]) return DQ_OK;
+  auto kern = bf16_gemm2_kernel<BM, FMT>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
       cudaSuccess)
     return DQ_ERR_LAUNCH;
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = bf16_pair_config<BM>(attr, nullptr);
+  cudaLaunchConfig_t cfg = bf16_pair_config<BM, FMT>(attr, nullptr);
   cfg.gridDim = dim3(2 * std::max(1, d->sms / 2));
   int clusters = 0;
   if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1)
     return DQ_ERR_LAUNCH;
-  d->bf16_max_pairs[bi] = clusters;
-  d->bf16_smem_set[bi] = 1;
+  d->bf16_max_pairs[FMT + 1][bi] = clusters;
+  d->bf16_smem_set[FMT + 1][bi] = 1;
   return DQ_OK;
 }
 
+template <int FMT>
 static int bf16_pair_capacity(DeviceInfo* d, int bm, int* pairs) {
   int rc = DQ_ERR_ARG;
   switch (bm) {
-    case 64: rc = bf16_pair_setup<64>(d); break;
-    case 128: rc = bf16_pair_setup<128>(d); break;
-    case 192: rc = bf16_pair_setup<192>(d); break;
-    case 256: rc = bf16_pair_setup<256>(d); break;
+    case 64: rc = bf16_pair_setup<64, FMT>(d); break;
+    case 128: rc = bf16_pair_setup<128, FMT>(d); break;
+    case 192: rc = bf16_pair_setup<192, FMT>(d); break;
+    case 256: rc = bf16_pair_setup<256, FMT>(d); break;
   }
-  if (rc == DQ_OK) *pairs = d->bf16_max_pairs[bm_index(bm)];
+  if (rc == DQ_OK) *pairs = d->bf16_max_pairs[FMT + 1][bm_index(bm)];
   return rc;
 }
 
-template <int BM>
+// FMT >= 0: the launch also decodes the weight (a.dq_*), its first weight
+// group just wide enough that the first wave of pairs finds all its tiles
+// there.  Every CTA must be resident at once (the producers wait for the
+// decode warps of all CTAs): the grid never exceeds the occupancy-derived
+// number of resident pairs.
+template <int BM, int FMT>
 static int launch_bf16_gemm2(DeviceInfo* d, const Plan& p, const CUtensorMap& mx,
                              const CUtensorMap& ma, const GemmArgs& a, cudaStream_t st) {
-  const int rc = bf16_pair_setup<BM>(d);
+  const int rc = bf16_pair_setup<BM, FMT>(d);
   if (rc != DQ_OK) return rc;
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = bf16_pair_config<BM>(attr, st);
-  const int pairs = std::max(1, std::min(p.grid, d->bf16_max_pairs[bm_index(BM)]));
+  cudaLaunchConfig_t cfg = bf16_pair_config<BM, FMT>(attr, st);
+  const int pairs = std::max(1, std::min(p.grid, d->bf16_max_pairs[FMT + 1][bm_index(BM)]));
   cfg.gridDim = dim3(2 * pairs);
-  if (cudaLaunchKernelEx(&cfg, bf16_gemm2_kernel<BM>, mx, ma, a) != cudaSuccess)
+  GemmArgs g = a;
+  if (FMT >= 0) {
+    const int m_tiles = std::max(1, p.m_tiles);
+    g.group0_n = std::min(a.group_n, std::max(1, (pairs + m_tiles - 1) / m_tiles));
+  }
+  if (cudaLaunchKernelEx(&cfg, bf16_gemm2_kernel<BM, FMT>, mx, ma, g) != cudaSuccess)
     return DQ_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
+}
+
+template <int FMT>
+static int launch_bf16_gemm2_bm(DeviceInfo* d, const Plan& p, const CUtensorMap& mx,
+                                const CUtensorMap& ma, const GemmArgs& a, cudaStream_t st) {
+  switch (p.bm) {
+    case 64: return launch_bf16_gemm2<64, FMT>(d, p, mx, ma, a, st);
+    case 128: return launch_bf16_gemm2<128, FMT>(d, p, mx, ma, a, st);
+    case 192: return launch_bf16_gemm2<192, FMT>(d, p, mx, ma, a, st);
+    case 256: return launch_bf16_gemm2<256, FMT>(d, p, mx, ma, a, st);
+  }
+  return DQ_ERR_ARG;
 }
 
 template <int FMT, bool TP>
@@ -536,7 +573,8 @@ static constexpr unsigned long long kTpWaitNs = 5000000000ull;  // 5 s
 static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8_t* w,
                        const float* absmax, float scale, const void* bias, int64_t N, void* y,
                        void* ws, size_t ws_bytes, cudaStream_t st, const TpOpts* tp = nullptr,
-                       bool allow_twophase = true) {
+                       bool allow_twophase = true, int act = kActNone) {
+  if (act != kActNone && act != kActGeluTanh) return DQ_ERR_ARG;
   // NF4 blocks of 64 must lie inside a weight row; fp8 needs only 16-byte
   // row strides for TMA (the ragged last k-block is zero-filled).
   if (M < 0 || N <= 0 || K <= 0 || (K % (fmt == kFmtNF4 ? 64 : 16)) != 0) return DQ_ERR_SHAPE;
@@ -554,17 +592,27 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
   if (p.ws > 0 && (ws == nullptr || ws_bytes < p.ws || !aligned(ws, 16))) return DQ_ERR_WORKSPACE;
 
   if (p.twophase) {
-    // phase 1: the weight, dequantized once into the bf16 scratch [N, K]
-    const int64_t n_elems = N * K;
-    if (fmt == kFmtNF4) {
-      dequant_nf4_kernel<<<grid_for(n_elems / 32, 256, d->sms), 256, 0, st>>>(
-          reinterpret_cast<const uint4*>(w), absmax, static_cast<uint4*>(ws), n_elems / 32);
-    } else {
-      dequant_fp8_kernel<<<grid_for(n_elems / 16 + 1, 256, d->sms), 256, 0, st>>>(
-          w, scale, static_cast<__nv_bfloat16*>(ws), n_elems);
+    // The weight is dequantized once into the bf16 scratch [N, K] and read
+    // by a bf16 x bf16 pair GEMM.  Normally the GEMM launch decodes it
+    // itself, group by group under the MMAs (the ready counters after the
+    // scratch start at zero); pair mode 4 runs the decode as its own launch
+    // first.
+    const bool separate = g_override_pair.load() == 4;
+    unsigned int* ready =
+        reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(ws) + twophase_counter_offset(N, K));
+    if (separate) {
+      const int64_t n_elems = N * K;
+      if (fmt == kFmtNF4) {
+        dequant_nf4_kernel<<<grid_for(n_elems / 32, 256, d->sms), 256, 0, st>>>(
+            reinterpret_cast<const uint4*>(w), absmax, static_cast<uint4*>(ws), n_elems / 32);
+      } else {
+        dequant_fp8_kernel<<<grid_for(n_elems / 16 + 1, 256, d->sms), 256, 0, st>>>(
+            w, scale, static_cast<__nv_bfloat16*>(ws), n_elems);
+      }
+      if (cudaGetLastError() != cudaSuccess) return DQ_ERR_LAUNCH;
+    } else if (cudaMemsetAsync(ready, 0, twophase_counter_bytes(p.n_tiles), st) != cudaSuccess) {
+      return DQ_ERR_CUDA;
     }
-    if (cudaGetLastError() != cudaSuccess) return DQ_ERR_LAUNCH;
-    // phase 2: bf16 x bf16 pair GEMM
     CUtensorMap mx2, ma;
     if (!make_map_2d(&mx2, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, M, K * 2, 64, p.bm / 2,
                      CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -572,7 +620,7 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
                      CU_TENSOR_MAP_SWIZZLE_128B))
       return DQ_ERR_CUDA;
     GemmArgs g;
-    g.absmax = nullptr;
+    g.absmax = absmax;
     g.bias = static_cast<const __nv_bfloat16*>(bias);
     g.out = nullptr;
     g.M = static_cast<int>(M);
@@ -583,8 +631,13 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
     g.num_tiles = p.tiles;
     g.splits = 1;
     g.kb_per_split = p.kb_per_split;
-    g.group_n = 16;  // the bf16 weight (N*K*2 bytes) no longer fits L2 beside X and Y
-    g.fp8_scale = 0.f;
+    g.group_n = kTwoPhaseGroupN;  // the bf16 weight no longer fits L2 beside X and Y
+    g.group0_n = 0;
+    g.act = act;
+    g.fp8_scale = scale;
+    g.dq_w = w;
+    g.dq_out = static_cast<__nv_bfloat16*>(ws);
+    g.dq_ready = ready;
     for (int r = 0; r < kMaxRanks; ++r) {
       g.outs[r] = nullptr;
       g.tp_flags[r] = nullptr;
@@ -597,13 +650,9 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
     g.tp_counter = nullptr;
     g.tp_rank = 0;
     g.tp_epoch = 0;
-    switch (p.bm) {
-      case 64: return launch_bf16_gemm2<64>(d, p, mx2, ma, g, st);
-      case 128: return launch_bf16_gemm2<128>(d, p, mx2, ma, g, st);
-      case 192: return launch_bf16_gemm2<192>(d, p, mx2, ma, g, st);
-      case 256: return launch_bf16_gemm2<256>(d, p, mx2, ma, g, st);
-    }
-    return DQ_ERR_ARG;
+    if (separate) return launch_bf16_gemm2_bm<-1>(d, p, mx2, ma, g, st);
+    return fmt == kFmtNF4 ? launch_bf16_gemm2_bm<kFmtNF4>(d, p, mx2, ma, g, st)
+                          : launch_bf16_gemm2_bm<kFmtFP8>(d, p, mx2, ma, g, st);
   }
 
   CUtensorMap mx, mw;
@@ -628,6 +677,11 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
   a.splits = p.splits;
   a.kb_per_split = p.kb_per_split;
   a.group_n = 0;
+  a.group0_n = 0;
+  a.dq_w = nullptr;
+  a.dq_out = nullptr;
+  a.dq_ready = nullptr;
+  a.act = act;
   a.fp8_scale = scale;
   for (int r = 0; r < kMaxRanks; ++r) {
     a.outs[r] = nullptr;
@@ -675,7 +729,7 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
     const int64_t total = M * N;
     splitk_reduce_kernel<<<grid_for(total, 256, d->sms), 256, 0, st>>>(
         static_cast<const float*>(ws), p.splits, a.M, a.N, a.bias,
-        static_cast<__nv_bfloat16*>(y));
+        static_cast<__nv_bfloat16*>(y), a.act);
     if (cudaGetLastError() != cudaSuccess) return DQ_ERR_LAUNCH;
   }
   if (tp != nullptr) {
@@ -812,6 +866,20 @@ size_t dq_workspace_size(int64_t M, int64_t N, int64_t K, int fmt) {
   return make_plan(M, N, K, d->sms).ws;
 }
 
+int dq_linear_nf4_ex(const void* x, int64_t M, int64_t K, const uint8_t* packed,
+                     const float* absmax, const void* bias, int64_t N, int act, void* y,
+                     void* workspace, size_t workspace_bytes, dq_stream_t stream) {
+  return linear_impl(kFmtNF4, x, M, K, packed, absmax, 0.f, bias, N, y, workspace, workspace_bytes,
+                     static_cast<cudaStream_t>(stream), nullptr, true, act);
+}
+
+int dq_linear_fp8_ex(const void* x, int64_t M, int64_t K, const uint8_t* w8, float scale,
+                     const void* bias, int64_t N, int act, void* y, void* workspace,
+                     size_t workspace_bytes, dq_stream_t stream) {
+  return linear_impl(kFmtFP8, x, M, K, w8, nullptr, scale, bias, N, y, workspace, workspace_bytes,
+                     static_cast<cudaStream_t>(stream), nullptr, true, act);
+}
+
 int dq_plan_info(int64_t M, int64_t N, int64_t K, int fmt, int* pair, int* bm, int* splits,
                  int* grid) {
   if (pair == nullptr || bm == nullptr || splits == nullptr || grid == nullptr) return DQ_ERR_ARG;
@@ -828,7 +896,9 @@ int dq_plan_info(int64_t M, int64_t N, int64_t K, int fmt, int* pair, int* bm, i
   *grid = p.grid;
   if (p.twophase) {
     int cap = 0;
-    const int prc = bf16_pair_capacity(d, p.bm, &cap);
+    const int prc = g_override_pair.load() == 4 ? bf16_pair_capacity<-1>(d, p.bm, &cap)
+                    : fmt == DQ_FMT_NF4         ? bf16_pair_capacity<kFmtNF4>(d, p.bm, &cap)
+                                                : bf16_pair_capacity<kFmtFP8>(d, p.bm, &cap);
     if (prc != DQ_OK) return prc;
     *grid = 2 * std::max(1, std::min(p.grid, cap));
   } else if (p.pair) {
@@ -1031,7 +1101,7 @@ int dq_device_error(int* code, dq_stream_t stream) {
 }
 
 int dq_set_pair_mode(int mode) {
-  if (mode < 0 || mode > 3) return DQ_ERR_ARG;
+  if (mode < 0 || mode > 4) return DQ_ERR_ARG;
   g_override_pair.store(mode);
   return DQ_OK;
 }

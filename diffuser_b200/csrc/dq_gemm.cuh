@@ -82,6 +82,7 @@ struct GemmArgs {
   int tile_n;                 // weight rows per tile: 128 (one CTA) or 256 (CTA pair)
   int splits, kb_per_split;
   int group_n;                // > 0: tiles visit group_n weight tiles x all token tiles at a time
+  int act;                    // kActNone or kActGeluTanh (bf16 output only)
   float fp8_scale;            // fp8: per-tensor scale (rounded to bf16 in-kernel)
   int vec_ok;                 // 16-byte vector stores are aligned for every destination
   // bf16 Y destinations (splits == 1): element (m, n) goes to
@@ -97,6 +98,16 @@ struct GemmArgs {
   unsigned int* tp_flags[kMaxRanks];
   int tp_rank;
   unsigned int tp_epoch;
+  // Grouped order: the first group spans group0_n weight tiles (<= group_n;
+  // 0 means group_n), the later ones group_n.
+  int group0_n;
+  // bf16 pair GEMM that dequantizes its own weight (bf16_gemm2_kernel<BM,
+  // FMT>, FMT >= 0): dq_w is the packed NF4 / e4m3 weight (with absmax or
+  // fp8_scale above), dq_out the bf16 scratch [N, K] its TMA loads read, and
+  // dq_ready[g] counts the dequantizing warps that finished weight group g.
+  const uint8_t* dq_w;
+  __nv_bfloat16* dq_out;
+  unsigned int* dq_ready;
 };
 
 // Column-parallel completion signal (every thread of the CTA calls it after
@@ -180,22 +191,41 @@ struct GemmCfg {
 
 struct TileCoord {
   int m0, n0, kb0, kb1, split;
+  int group;  // weight group of the grouped order (0 otherwise)
 };
+
+// Width of the first weight group of the grouped order.
+__host__ __device__ __forceinline__ int first_group_width(int group_n, int group0_n, int n_tiles) {
+  const int g0 = group0_n > 0 ? (group0_n < group_n ? group0_n : group_n) : group_n;
+  return g0 < n_tiles ? g0 : n_tiles;
+}
 
 __device__ __forceinline__ TileCoord tile_coord(const GemmArgs& a, int t, int KB) {
   TileCoord c;
   c.split = t % a.splits;
+  c.group = 0;
   const int mn = t / a.splits;
   if (a.group_n > 0) {
-    // Grouped order: token tiles run fastest over a group of group_n weight
-    // tiles, so the tiles in flight share a few weight tiles (kept in L2)
-    // instead of streaming every weight row once per token tile.
+    // Grouped order: token tiles run fastest over a group of weight tiles, so
+    // the tiles in flight share a few weight tiles (kept in L2) instead of
+    // streaming every weight row once per token tile.  The first group may be
+    // narrower (group0_n) so that the weight it needs is ready sooner.
     const int m_tiles = a.num_tiles / (a.splits * a.num_n_tiles);
-    const int per_group = a.group_n * m_tiles;
-    const int g = mn / per_group;
-    const int r = mn - g * per_group;
-    const int gn = min(a.group_n, a.num_n_tiles - g * a.group_n);
-    c.n0 = (g * a.group_n + r % gn) * a.tile_n;
+    const int g0 = first_group_width(a.group_n, a.group0_n, a.num_n_tiles);
+    int nb, gn, r;
+    if (mn < g0 * m_tiles) {
+      nb = 0;
+      gn = g0;
+      r = mn;
+    } else {
+      const int per_group = a.group_n * m_tiles;
+      const int q = (mn - g0 * m_tiles) / per_group;
+      c.group = 1 + q;
+      nb = g0 + q * a.group_n;
+      gn = min(a.group_n, a.num_n_tiles - nb);
+      r = mn - g0 * m_tiles - q * per_group;
+    }
+    c.n0 = (nb + r % gn) * a.tile_n;
     c.m0 = r / gn;
   } else {
     c.n0 = (mn % a.num_n_tiles) * a.tile_n;
@@ -585,10 +615,18 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
           // instantiation; the store loop is compiled only there: even an
           // untaken one costs ~10% at BM=256, where the drain is exposed)
           __nv_bfloat16* sb = reinterpret_cast<__nv_bfloat16*>(stg);
+          if (args.act == kActNone) {
 #pragma unroll
-          for (int j = 0; j < EC; ++j)
-            sts16(stg_s + 2u * (j * 32 + lane),
-                  __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(vc[j]) + bias)));
+            for (int j = 0; j < EC; ++j)
+              sts16(stg_s + 2u * (j * 32 + lane),
+                    __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(vc[j]) + bias)));
+          } else {
+#pragma unroll
+            for (int j = 0; j < EC; ++j)
+              sts16(stg_s + 2u * (j * 32 + lane),
+                    __bfloat16_as_ushort(__float2bfloat16_rn(
+                        apply_act(__uint_as_float(vc[j]) + bias, args.act))));
+          }
           __syncwarp();
 #pragma unroll
           for (int i = 0; i < EC / 8; ++i) {

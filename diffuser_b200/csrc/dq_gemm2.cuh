@@ -411,10 +411,18 @@ __global__ void __launch_bounds__(Gemm2Cfg<FMT, BM>::kThreads, 1)
           // instantiation; the store loop is compiled only there: even an
           // untaken one costs ~10% at BM=256, where the drain is exposed)
           __nv_bfloat16* sb = reinterpret_cast<__nv_bfloat16*>(stg);
+          if (args.act == kActNone) {
 #pragma unroll
-          for (int j = 0; j < EC; ++j)
-            sts16(stg_s + 2u * (j * 32 + lane),
-                  __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(vc[j]) + bias)));
+            for (int j = 0; j < EC; ++j)
+              sts16(stg_s + 2u * (j * 32 + lane),
+                    __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(vc[j]) + bias)));
+          } else {
+#pragma unroll
+            for (int j = 0; j < EC; ++j)
+              sts16(stg_s + 2u * (j * 32 + lane),
+                    __bfloat16_as_ushort(__float2bfloat16_rn(
+                        apply_act(__uint_as_float(vc[j]) + bias, args.act))));
+          }
           __syncwarp();
 #pragma unroll
           for (int i = 0; i < EC / 8; ++i) {

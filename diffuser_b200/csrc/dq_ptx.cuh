@@ -66,6 +66,39 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Orders this thread's generic-proxy view of global memory against its
+// async-proxy (TMA) accesses: data that other threads wrote with ordinary
+// stores, acquired through a counter, is then seen by the TMA loads issued
+// after the fence.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+__device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait until the global counter *p reaches target (acquire).  Gives
+// up after limit_ns (or when another role of the CTA gave up): sets
+// *abort_flag and returns false.
+__device__ __forceinline__ bool wait_count_geq(const unsigned int* p, unsigned int target,
+                                               volatile int* abort_flag,
+                                               unsigned long long limit_ns = kWaitTimeoutNs) {
+  if (ld_acquire_gpu(p) >= target) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (true) {
+    __nanosleep(64);
+    if (ld_acquire_gpu(p) >= target) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > limit_ns) {
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }

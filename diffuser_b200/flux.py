@@ -68,6 +68,19 @@ def heads_to_tokens(x, s_txt: int):
     return txt, img
 
 
+# GELU-tanh after the up-projections runs in the quantized linear's epilogue
+# (False: a separate activation pass, as the reference does).
+FUSED_GELU = True
+
+
+def _proj_gelu_tanh(proj, x):
+    """GELU-tanh of a projection; fused into the quantized linear's epilogue on
+    the engine (the projection is still rounded to bf16 before the activation)."""
+    if FUSED_GELU and isinstance(proj, (modules.Ltx23Nf4Linear, modules.Ltx23Fp8Linear)) and x.is_cuda:
+        return proj(x, act="gelu_tanh")
+    return F.gelu(proj(x), approximate="tanh")
+
+
 # --------------------------------------------------------------- primitives
 class RMSNorm(nn.Module):
     """ltx23_rms_norm (R/dit_ltx23_modules.R:25-46): normalize in float32, then
@@ -131,7 +144,7 @@ class GeluProj(nn.Module):
         self.proj = nn.Linear(dim_in, dim_out)
 
     def forward(self, x):
-        return F.gelu(self.proj(x), approximate="tanh")
+        return _proj_gelu_tanh(self.proj, x)
 
 
 class FeedForward(nn.Module):
@@ -338,7 +351,7 @@ class SingleBlock(nn.Module):
 
     def forward(self, x, temb, rope):
         n, gate = self.norm(x, temb)
-        mlp = F.gelu(self.proj_mlp(n), approximate="tanh")
+        mlp = _proj_gelu_tanh(self.proj_mlp, n)
         a = self.attn(n, rope=rope)
         x = x + gate[:, None] * self.proj_out(torch.cat([a, mlp], dim=2))
         if x.dtype == torch.float16:

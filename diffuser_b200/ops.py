@@ -172,9 +172,13 @@ def _prep_bias(bias, n: int, device):
     return b.contiguous()
 
 
+_ACTS = {None: _lib.DQ_ACT_NONE, "gelu_tanh": _lib.DQ_ACT_GELU_TANH}
+
+
 def nf4_linear(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor,
-               out_features: int, bias: torch.Tensor | None = None) -> torch.Tensor:
-    """y = x . dequant_nf4(W)^T + bias in one fused kernel (R/nf4_ltx23.R:235-246)."""
+               out_features: int, bias: torch.Tensor | None = None, act: str | None = None) -> torch.Tensor:
+    """y = x . dequant_nf4(W)^T + bias (R/nf4_ltx23.R:235-246); act="gelu_tanh"
+    applies GELU-tanh in the epilogue, as gelu_proj does after the projection."""
     n = int(out_features)
     k = packed.numel() * 2 // n
     x2 = _prep_x(x, k)
@@ -185,15 +189,21 @@ def nf4_linear(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor,
     with torch.cuda.device(x.device):
         ws_bytes = workspace_size(m, n, k, _lib.DQ_FMT_NF4)
         ws = workspace(x.device, ws_bytes)
-        _lib.check("dq_linear_nf4", _lib.lib().dq_linear_nf4(
-            _ptr(x2), m, k, _ptr(packed), _ptr(am), _ptr(b), n, _ptr(y),
-            _ptr(ws), ws_bytes, _stream(x.device)))
+        if act is None:
+            _lib.check("dq_linear_nf4", _lib.lib().dq_linear_nf4(
+                _ptr(x2), m, k, _ptr(packed), _ptr(am), _ptr(b), n, _ptr(y),
+                _ptr(ws), ws_bytes, _stream(x.device)))
+        else:
+            _lib.check("dq_linear_nf4_ex", _lib.lib().dq_linear_nf4_ex(
+                _ptr(x2), m, k, _ptr(packed), _ptr(am), _ptr(b), n, _ACTS[act], _ptr(y),
+                _ptr(ws), ws_bytes, _stream(x.device)))
     return y.reshape(*x.shape[:-1], n)
 
 
 def fp8_linear(x: torch.Tensor, w8: torch.Tensor, scale: float,
-               bias: torch.Tensor | None = None) -> torch.Tensor:
-    """y = x . (e4m3(W) * bf16(scale))^T + bias fused (R/fp8_ltx23.R:70-83)."""
+               bias: torch.Tensor | None = None, act: str | None = None) -> torch.Tensor:
+    """y = x . (e4m3(W) * bf16(scale))^T + bias fused (R/fp8_ltx23.R:70-83);
+    act="gelu_tanh" applies GELU-tanh in the epilogue."""
     n, k = int(w8.shape[0]), int(w8.shape[1])
     x2 = _prep_x(x, k)
     m = x2.shape[0]
@@ -203,9 +213,14 @@ def fp8_linear(x: torch.Tensor, w8: torch.Tensor, scale: float,
     with torch.cuda.device(x.device):
         ws_bytes = workspace_size(m, n, k, _lib.DQ_FMT_FP8)
         ws = workspace(x.device, ws_bytes)
-        _lib.check("dq_linear_fp8", _lib.lib().dq_linear_fp8(
-            _ptr(x2), m, k, _ptr(raw), ctypes.c_float(float(scale)), _ptr(b), n, _ptr(y),
-            _ptr(ws), ws_bytes, _stream(x.device)))
+        if act is None:
+            _lib.check("dq_linear_fp8", _lib.lib().dq_linear_fp8(
+                _ptr(x2), m, k, _ptr(raw), ctypes.c_float(float(scale)), _ptr(b), n, _ptr(y),
+                _ptr(ws), ws_bytes, _stream(x.device)))
+        else:
+            _lib.check("dq_linear_fp8_ex", _lib.lib().dq_linear_fp8_ex(
+                _ptr(x2), m, k, _ptr(raw), ctypes.c_float(float(scale)), _ptr(b), n, _ACTS[act],
+                _ptr(y), _ptr(ws), ws_bytes, _stream(x.device)))
     return y.reshape(*x.shape[:-1], n)
 
 
@@ -220,7 +235,9 @@ def device_error(device=None) -> int:
 
 def set_pair_mode(mode: int = 0) -> None:
     """0 = automatic, 1 = fused one-CTA tiles, 2 = fused CTA-pair tiles,
-    3 = two-phase (dequantize into bf16 scratch, then the bf16 pair GEMM)."""
+    3 = two-phase (the bf16 pair GEMM launch dequantizes the weight into bf16
+    scratch one group of weight tiles ahead of its MMAs), 4 = two-phase with
+    the dequantization as a separate launch before the GEMM."""
     _lib.check("dq_set_pair_mode", _lib.lib().dq_set_pair_mode(int(mode)))
 
 
@@ -236,6 +253,6 @@ def plan_info(M: int, N: int, K: int, fmt: int = _lib.DQ_FMT_NF4) -> dict:
                                                        *[ctypes.byref(v) for v in vals]))
     pair, bm, splits, grid = (v.value for v in vals)
     kernel = {0: "dq_gemm_kernel (one CTA)", 1: "dq_gemm2_kernel (CTA pair)",
-              2: "bf16_gemm2_kernel (CTA pair) after dequant"}[pair]
+              2: "bf16_gemm2_kernel (CTA pair, decoding its weight in-launch)"}[pair]
     return {"kernel": kernel, "pair": pair >= 1, "twophase": pair == 2, "bm": bm, "splits": splits,
             "grid": grid}

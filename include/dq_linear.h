@@ -83,8 +83,10 @@ int dq_dequant_fp8(const uint8_t* w8, float scale, int64_t n_elems,
 
 /* ------------------------------------------------------------------ linear
  * Bytes of caller-provided scratch the linear needs for this shape: split-K
- * partial sums for small token counts, the bf16 weight (N*K*2) for the
- * two-phase plan of large ones, else 0. */
+ * partial sums for small token counts; for the two-phase plan of large ones
+ * the bf16 weight (N*K*2, rounded up to 256) followed by the weight groups'
+ * ready counters (4 * (N/256 + 2) bytes, rounded up to 256); else 0.  The
+ * contents need no initialization. */
 size_t dq_workspace_size(int64_t M, int64_t N, int64_t K, int fmt);
 
 /* y = x . dequant(W)^T + bias, dequantization fused into a tcgen05 GEMM.
@@ -132,8 +134,10 @@ int dq_set_tile_override(int bm, int splits);
 
 /* Kernel-family override for benchmarking: 0 = automatic, 1 = fused, one CTA
  * per tile (128 weight rows), 2 = fused, CTA-pair tiles (256 weight rows,
- * x-tile >= 64), 3 = two-phase: dequantize the weight once into bf16 scratch
- * (part of the workspace), then a bf16 CTA-pair GEMM (automatic for M >= 1024). */
+ * x-tile >= 64), 3 = two-phase: the weight dequantized once into bf16 scratch
+ * (part of the workspace) by the bf16 CTA-pair GEMM launch itself, one group
+ * of weight tiles ahead of its MMAs (automatic for M >= 1024), 4 = two-phase
+ * with the dequantization as a separate launch before the GEMM. */
 int dq_set_pair_mode(int mode);
 
 /* ------------------------------------------------- column-parallel linear
@@ -172,6 +176,19 @@ int dq_tp_linear_fp8(const void* x, int64_t M, int64_t K, const uint8_t* w8_shar
                      const void* bias_shard, int64_t N, int rank, int world, void* const* y_ranks,
                      unsigned int* const* flag_ranks, unsigned int* counter, unsigned int epoch,
                      dq_stream_t stream);
+
+/* The linears with an activation fused into the epilogue: act = DQ_ACT_NONE or
+ * DQ_ACT_GELU_TANH, y = bf16(gelu_tanh(bf16(x . W^T + bias))).  Replaces the
+ * reference's up-projection followed by nnf_gelu(approximate = "tanh")
+ * (ltx23_feed_forward's gelu_proj, R/dit_ltx23_modules.R:500-516, and the
+ * FLUX single block's proj_mlp, R/dit_flux_modules.R:311). */
+enum { DQ_ACT_NONE = 0, DQ_ACT_GELU_TANH = 1 };
+int dq_linear_nf4_ex(const void* x, int64_t M, int64_t K, const uint8_t* packed,
+                     const float* absmax, const void* bias, int64_t N, int act, void* y,
+                     void* workspace, size_t workspace_bytes, dq_stream_t stream);
+int dq_linear_fp8_ex(const void* x, int64_t M, int64_t K, const uint8_t* w8, float scale,
+                     const void* bias, int64_t N, int act, void* y, void* workspace,
+                     size_t workspace_bytes, dq_stream_t stream);
 
 /* Describes the launch plan dq_linear_* uses for this shape on the current
  * device: *pair = 0 for fused one-CTA tiles (128 weight rows), 1 for fused

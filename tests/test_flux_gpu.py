@@ -37,9 +37,11 @@ class _ReferenceBackend:
                     buffers[key] = torch.empty(key, dtype=torch.bfloat16, device=m.weight_nf4.device)
                 buf = buffers[key]
 
-                def fwd(x, m=m, buf=buf):
-                    return T.nf4_linear_forward(x, m.weight_nf4, m.weight_absmax, m.out_features,
-                                                m.in_features, m.bias, w_buffer=buf)
+                def fwd(x, act=None, m=m, buf=buf):
+                    y = T.nf4_linear_forward(x, m.weight_nf4, m.weight_absmax, m.out_features,
+                                             m.in_features, m.bias, w_buffer=buf)
+                    # the reference applies nnf_gelu(approximate = "tanh") after the linear
+                    return torch.nn.functional.gelu(y, approximate="tanh") if act else y
                 self.saved.append((m, m.forward))
                 m.forward = fwd
 

@@ -84,13 +84,15 @@ def test_every_tile_height(ops, fmt, bm):
     assert R.rel_err(to_bits(y), ref) <= TOL
 
 
+@pytest.mark.parametrize("mode", [3, 4])
 @pytest.mark.parametrize("fmt", ["nf4", "fp8"])
 @pytest.mark.parametrize("bm", [64, 128, 192, 256])
 @pytest.mark.parametrize("m,n,k", [(300, 640, 512), (1000, 136, 1088), (70, 264, 3072)])
-def test_two_phase(ops, fmt, bm, m, n, k):
-    # dequantize once into bf16 scratch, then the bf16 CTA-pair GEMM
+def test_two_phase(ops, mode, fmt, bm, m, n, k):
+    # dequantize once into bf16 scratch, then the bf16 CTA-pair GEMM: inside
+    # the GEMM launch (mode 3) or as a launch of its own (mode 4)
     x, w, bias, ref = _case(m, n, k, 3 * bm + n, fmt, with_bias=True)
-    ops.set_pair_mode(3)
+    ops.set_pair_mode(mode)
     ops.set_tile_override(bm, 0)
     try:
         assert ops.plan_info(m, n, k, 0 if fmt == "nf4" else 1)["twophase"]
@@ -100,6 +102,22 @@ def test_two_phase(ops, fmt, bm, m, n, k):
         ops.set_tile_override(0, 0)
         ops.set_pair_mode(0)
     assert R.rel_err(to_bits(y), ref) <= TOL
+
+
+@pytest.mark.parametrize("fmt", ["nf4", "fp8"])
+@pytest.mark.parametrize("m,n,k", [(4608, 6000, 128), (2048, 12800, 64), (1100, 300, 4096)])
+def test_two_phase_weight_groups(ops, fmt, m, n, k):
+    # the in-launch decode walks the weight in groups of the tile order (a
+    # narrow first group, then 16 weight tiles): several groups, a ragged
+    # last weight tile, and a single group
+    x, w, bias, ref = _case(m, n, k, 11 + n, fmt, with_bias=True)
+    y = _run(ops, fmt, x, w, bias, n)
+    torch.cuda.synchronize()
+    assert ops.plan_info(m, n, k, 0 if fmt == "nf4" else 1)["twophase"]
+    assert R.rel_err(to_bits(y), ref) <= TOL
+    y2 = _run(ops, fmt, x, w, bias, n)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y2)
 
 
 @pytest.mark.parametrize("fmt", ["nf4", "fp8"])
@@ -191,7 +209,7 @@ def test_full_size_fp8(ops):
 
 @pytest.mark.parametrize("fmt", ["nf4", "fp8"])
 @pytest.mark.parametrize("mode,bm", [(1, 128), (1, 192), (1, 256), (2, 192), (2, 256),
-                                     (3, 128), (3, 256)])
+                                     (3, 128), (3, 256), (4, 256)])
 def test_full_size_every_plan(ops, fmt, mode, bm):
     # every tile plan at the benchmarked shape, twice: a pipeline race shows
     # up as a large or run-to-run varying error here
@@ -218,12 +236,48 @@ def test_golden_linear(ops):
     assert R.rel_err(to_bits(y2), g["fp8_y"]) <= TOL
 
 
+@pytest.mark.parametrize("fmt", ["nf4", "fp8"])
+@pytest.mark.parametrize("mode,bm,splits,m,n,k", [(1, 128, 0, 300, 640, 512),   # fused one-CTA
+                                                  (2, 192, 0, 300, 640, 512),   # fused pair
+                                                  (3, 256, 0, 300, 640, 512),   # two-phase
+                                                  (4, 256, 0, 300, 640, 512),   # two launches
+                                                  (1, 0, 3, 16, 640, 1088)])    # split-K reduce
+def test_gelu_tanh_epilogue(ops, fmt, mode, bm, splits, m, n, k):
+    # y = bf16(gelu_tanh(bf16(x W^T + b))) in the epilogue equals the linear
+    # followed by torch's GELU-tanh on its bf16 output (the reference's
+    # gelu_proj), up to the last bit of the activation arithmetic
+    x, w, bias, ref = _case(m, n, k, 97 + m, fmt, with_bias=True)
+    ops.set_pair_mode(mode)
+    ops.set_tile_override(bm, splits)
+    try:
+        y_plain = _run(ops, fmt, x, w, bias, n)
+        xc, bc = x.cuda(), bias.cuda()
+        if fmt == "nf4":
+            y_act = ops.nf4_linear(xc, w[0], w[1], n, bc, act="gelu_tanh")
+        else:
+            y_act = ops.fp8_linear(xc, w[0], w[1], bc, act="gelu_tanh")
+        torch.cuda.synchronize()
+    finally:
+        ops.set_tile_override(0, 0)
+        ops.set_pair_mode(0)
+    ref_act = torch.nn.functional.gelu(y_plain, approximate="tanh")
+    step = ref_act.float().abs() * 2.0 ** -7 + 1e-6
+    assert ((y_act.float() - ref_act.float()).abs() <= step).all()
+    assert (y_act != ref_act).float().mean().item() < 0.01
+    # and against the oracle's linear through the same activation
+    gelu_oracle = torch.nn.functional.gelu(
+        torch.from_numpy(ref.view(np.int16)).view(torch.bfloat16).float(), approximate="tanh")
+    err = (y_act.float().cpu() - gelu_oracle).abs().max() / gelu_oracle.abs().max()
+    assert err.item() <= TOL
+
+
 def test_plan_choice(ops):
     # large token batches dequantize once and run the bf16 pair GEMM,
     # mid-sized ones the fused kernels, decode-sized ones one-CTA tiles
     big = ops.plan_info(4608, 12288, 3072)
     assert big["twophase"] and big["bm"] == 256 and big["splits"] == 1
-    assert ops.workspace_size(4608, 12288, 3072) == 12288 * 3072 * 2
+    # the bf16 weight, then 256 bytes of weight-group counters
+    assert ops.workspace_size(4608, 12288, 3072) == 12288 * 3072 * 2 + 256
     mid = ops.plan_info(512, 12288, 3072)
     assert not mid["twophase"]
     small = ops.plan_info(16, 3072, 3072)
