@@ -18,6 +18,7 @@
 #include "dq_gemm2.cuh"
 #include "dq_bf16gemm2.cuh"
 #include "dq_dit.cuh"
+#include "dq_smallm.cuh"
 
 #define DQ_VERSION_STRING "dqlinear-b200 0.1.0 (sm_100a)"
 
@@ -173,6 +174,7 @@ struct DeviceInfo {
   int max_pairs[2][6] = {};     // [fmt][bm]
   int bf16_smem_set[3][6] = {};    // bf16 pair GEMM, [decoded format + 1][bm]
   int bf16_max_pairs[3][6] = {};
+  int smallm_set[2][2][3] = {};    // small-M kernel, [fmt][token tiles - 1][row groups 1/2/4]
 };
 
 constexpr int kMaxDevices = 64;
@@ -232,6 +234,7 @@ static bool make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType 
 struct Plan {
   bool pair = false;      // CTA-pair tiles (256 weight rows per tile)
   bool twophase = false;  // dequantize into bf16 scratch, then the bf16 pair GEMM
+  bool smallm = false;    // decode-sized M: register-decode warp MMAs (smallm_kernel)
   int bm = 0, splits = 1, kb_per_split = 0;
   int m_tiles = 0, n_tiles = 0, tiles = 0, grid = 0;
   size_t ws = 0;
@@ -259,6 +262,17 @@ struct TileShape {
 static constexpr TileShape kShapes[] = {
     {false, 128, 0.72}, {false, 192, 1.0}, {false, 256, 0.97}, {true, 192, 0.93}, {true, 256, 1.13}};
 
+// The small-M kernel serves M <= kSmallMMaxM (two 8-token tiles) with K a
+// multiple of 128.
+constexpr int64_t kSmallMMaxM = 16;
+// Row groups (16 weight rows each) per small-M CTA, so one CTA's LUT fill and
+// x loads serve more rows and more weight bytes are in flight per warp: the
+// most that still give every SM a CTA (measured: four for NF4 with one token
+// tile, two for fp8 and for two token tiles, whose registers run out).
+static int smallm_r16(int fmt, int64_t M, int64_t N, int sms) {
+  if (fmt == kFmtNF4 && M <= 8 && (N + 63) / 64 >= sms) return 4;
+  return (N + 31) / 32 >= sms ? 2 : 1;
+}
 // Token count from which the two-phase plan is chosen: decoding the weight
 // once (~N*K*2.6 bytes of HBM traffic) costs less than decoding it in every
 // token tile, and the bf16 pair GEMM runs faster than the fused kernels.
@@ -276,14 +290,32 @@ static size_t twophase_counter_bytes(int n_tiles) {
 // group's bf16 weight stays in L2 while the token tiles sweep past it).
 constexpr int kTwoPhaseGroupN = 16;
 
-static Plan make_plan(int64_t M, int64_t N, int64_t K, int sms, bool allow_split = true,
-                      bool allow_twophase = true) {
+static Plan make_plan(int fmt, int64_t M, int64_t N, int64_t K, int sms, bool allow_split = true,
+                      bool allow_twophase = true, bool allow_smallm = true) {
   Plan p;
   const int KB = static_cast<int>((K + 63) / 64);
   // 0 automatic, 1 one-CTA fused only, 2 CTA-pair fused only, 3 two-phase
-  // only, 4 two-phase only with the dequantization as its own launch
+  // only, 4 two-phase only with the dequantization as its own launch, 5 the
+  // small-M kernel wherever it applies
   const int opair = g_override_pair.load();
   const int obm = g_override_bm.load();
+  // Automatic for M <= 8 (one 8-token tile); for a second tile only with two
+  // row groups per CTA -- with one, the fused kernel is faster there.
+  if (allow_smallm && M <= kSmallMMaxM && K % 128 == 0 &&
+      (opair == 5 || (opair == 0 && obm == 0 && g_override_splits.load() == 0 &&
+                      (M <= 8 || smallm_r16(fmt, M, N, sms) >= 2)))) {
+    p.smallm = true;
+    p.bm = M <= 8 ? 8 : 16;
+    p.m_tiles = 1;
+    const int r16 = smallm_r16(fmt, M, N, sms);
+    p.n_tiles = static_cast<int>((N + 16 * r16 - 1) / (16 * r16));
+    p.tiles = p.n_tiles;
+    p.grid = p.n_tiles;
+    p.splits = 1;
+    p.kb_per_split = KB;
+    p.ws = 0;
+    return p;
+  }
   auto units_of = [&](bool pair) { return pair ? sms / 2 : sms; };
   auto n_tiles_of = [&](bool pair) { return static_cast<int>((N + (pair ? 255 : 127)) / (pair ? 256 : 128)); };
   const bool twophase = allow_twophase && M > 64 &&
@@ -570,6 +602,42 @@ struct TpOpts {
 
 static constexpr unsigned long long kTpWaitNs = 5000000000ull;  // 5 s
 
+// The small-M kernel: one CTA per 16 * R16 weight rows, MT 8-token tiles.
+template <int FMT, int MT, int R16>
+static int launch_smallm_cfg(DeviceInfo* d, const Plan& p, const void* x, const uint8_t* w,
+                             const float* absmax, float scale, const void* bias, void* y,
+                             int64_t M, int64_t N, int64_t K, int act, cudaStream_t st) {
+  using C = SmallMCfg<FMT, MT, R16>;
+  auto kern = smallm_kernel<FMT, MT, R16>;
+  int& set = d->smallm_set[FMT][MT - 1][R16 == 4 ? 2 : R16 - 1];
+  if (!set) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
+        cudaSuccess)
+      return DQ_ERR_LAUNCH;
+    set = 1;
+  }
+  kern<<<p.grid, C::kThreads, C::kSmemBytes, st>>>(
+      static_cast<const __nv_bfloat16*>(x), w, absmax, scale,
+      static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y),
+      static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), act);
+  return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
+}
+
+template <int FMT, int MT>
+static int launch_smallm(DeviceInfo* d, const Plan& p, const void* x, const uint8_t* w,
+                         const float* absmax, float scale, const void* bias, void* y, int64_t M,
+                         int64_t N, int64_t K, int act, cudaStream_t st) {
+  switch (smallm_r16(FMT, M, N, d->sms)) {
+    case 4:
+      if constexpr (MT == 1)
+        return launch_smallm_cfg<FMT, MT, 4>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, st);
+      break;
+    case 2:
+      return launch_smallm_cfg<FMT, MT, 2>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, st);
+  }
+  return launch_smallm_cfg<FMT, MT, 1>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, st);
+}
+
 static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8_t* w,
                        const float* absmax, float scale, const void* bias, int64_t N, void* y,
                        void* ws, size_t ws_bytes, cudaStream_t st, const TpOpts* tp = nullptr,
@@ -588,8 +656,17 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
   DeviceInfo* d = nullptr;
   int rc = current_device(&d);
   if (rc != DQ_OK) return rc;
-  const Plan p = make_plan(M, N, K, d->sms, tp == nullptr, allow_twophase && tp == nullptr);
+  const Plan p = make_plan(fmt, M, N, K, d->sms, tp == nullptr, allow_twophase && tp == nullptr,
+                           tp == nullptr);
   if (p.ws > 0 && (ws == nullptr || ws_bytes < p.ws || !aligned(ws, 16))) return DQ_ERR_WORKSPACE;
+
+  if (p.smallm) {
+    if (fmt == kFmtNF4)
+      return p.bm <= 8 ? launch_smallm<kFmtNF4, 1>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, st)
+                       : launch_smallm<kFmtNF4, 2>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, st);
+    return p.bm <= 8 ? launch_smallm<kFmtFP8, 1>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, st)
+                     : launch_smallm<kFmtFP8, 2>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, st);
+  }
 
   if (p.twophase) {
     // The weight is dequantized once into the bf16 scratch [N, K] and read
@@ -863,7 +940,7 @@ size_t dq_workspace_size(int64_t M, int64_t N, int64_t K, int fmt) {
   if (M <= 0 || N <= 0 || K <= 0 || (K % (fmt == DQ_FMT_NF4 ? 64 : 16)) != 0) return 0;
   DeviceInfo* d = nullptr;
   if (current_device(&d) != DQ_OK || d == nullptr) return 0;
-  return make_plan(M, N, K, d->sms).ws;
+  return make_plan(fmt, M, N, K, d->sms).ws;
 }
 
 int dq_linear_nf4_ex(const void* x, int64_t M, int64_t K, const uint8_t* packed,
@@ -889,8 +966,8 @@ int dq_plan_info(int64_t M, int64_t N, int64_t K, int fmt, int* pair, int* bm, i
   DeviceInfo* d = nullptr;
   const int rc = current_device(&d);
   if (rc != DQ_OK) return rc;
-  const Plan p = make_plan(M, N, K, d->sms);
-  *pair = p.twophase ? 2 : (p.pair ? 1 : 0);
+  const Plan p = make_plan(fmt, M, N, K, d->sms);
+  *pair = p.smallm ? 3 : p.twophase ? 2 : (p.pair ? 1 : 0);
   *bm = p.bm;
   *splits = p.splits;
   *grid = p.grid;
@@ -946,7 +1023,7 @@ int dq_linear_nf4_noalloc(const void* x, int64_t M, int64_t K, const uint8_t* pa
   DeviceInfo* d = nullptr;
   int rc = current_device(&d);
   if (rc != DQ_OK) return rc;
-  if (make_plan(M, N, K, d->sms, true, false).ws > DQ_NOALLOC_SCRATCH_BYTES)
+  if (make_plan(kFmtNF4, M, N, K, d->sms, true, false).ws > DQ_NOALLOC_SCRATCH_BYTES)
     return DQ_ERR_SCRATCH_LIMIT;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return DQ_ERR_CUDA;
@@ -1101,7 +1178,7 @@ int dq_device_error(int* code, dq_stream_t stream) {
 }
 
 int dq_set_pair_mode(int mode) {
-  if (mode < 0 || mode > 4) return DQ_ERR_ARG;
+  if (mode < 0 || mode > 5) return DQ_ERR_ARG;
   g_override_pair.store(mode);
   return DQ_OK;
 }

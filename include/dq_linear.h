@@ -137,7 +137,9 @@ int dq_set_tile_override(int bm, int splits);
  * x-tile >= 64), 3 = two-phase: the weight dequantized once into bf16 scratch
  * (part of the workspace) by the bf16 CTA-pair GEMM launch itself, one group
  * of weight tiles ahead of its MMAs (automatic for M >= 1024), 4 = two-phase
- * with the dequantization as a separate launch before the GEMM. */
+ * with the dequantization as a separate launch before the GEMM, 5 = the
+ * small-M kernel (weights decoded into warp-MMA registers; M <= 16 and
+ * K % 128 == 0, automatic for M <= 8 and for M <= 16 when N >= 32 * SMs). */
 int dq_set_pair_mode(int mode);
 
 /* ------------------------------------------------- column-parallel linear
@@ -193,7 +195,8 @@ int dq_linear_fp8_ex(const void* x, int64_t M, int64_t K, const uint8_t* w8, flo
 /* Describes the launch plan dq_linear_* uses for this shape on the current
  * device: *pair = 0 for fused one-CTA tiles (128 weight rows), 1 for fused
  * CTA-pair tiles (256 rows), 2 for the two-phase plan (dequantize, then the
- * bf16 pair GEMM); *bm = x-tile rows, *splits = split-K count, *grid = CTAs
+ * bf16 pair GEMM), 3 for the small-M kernel (*bm = 8 or 16 tokens, 16, 32 or
+ * 64 weight rows per CTA); *bm = x-tile rows, *splits = split-K count, *grid = CTAs
  * launched.  A diagnostic query with no reference counterpart. */
 int dq_plan_info(int64_t M, int64_t N, int64_t K, int fmt, int* pair, int* bm, int* splits,
                  int* grid);

@@ -141,14 +141,43 @@ def test_cta_pair_tiles(ops, fmt, bm, m, n, k):
 @pytest.mark.parametrize("m,n,k,splits", [(1, 1024, 4096, 0), (16, 3072, 3072, 0),
                                           (64, 2304, 3072, 5), (3, 200, 1088, 3)])
 def test_split_k(ops, fmt, m, n, k, splits):
+    # the fused one-CTA kernel with K split across CTAs (automatic count when
+    # splits == 0) and the f32 reduce kernel
     x, w, bias, ref = _case(m, n, k, 17 + m, fmt, with_bias=True)
+    ops.set_pair_mode(1)
     ops.set_tile_override(0, splits)
     try:
+        assert ops.plan_info(m, n, k, 0 if fmt == "nf4" else 1)["splits"] > 1
         y = _run(ops, fmt, x, w, bias, n)
         torch.cuda.synchronize()
     finally:
         ops.set_tile_override(0, 0)
+        ops.set_pair_mode(0)
     assert R.rel_err(to_bits(y), ref) <= TOL
+
+
+@pytest.mark.parametrize("fmt", ["nf4", "fp8"])
+@pytest.mark.parametrize("m,n,k,with_bias", [(1, 64, 128, True), (3, 200, 384, False),
+                                             (8, 3072, 3072, True), (9, 136, 1024, True),
+                                             (16, 1000, 1152, False), (16, 18432, 3072, True),
+                                             (2, 3072, 15360, True), (5, 9000, 256, True),
+                                             (1, 18432, 512, False)])
+def test_small_m_kernel(ops, fmt, m, n, k, with_bias):
+    # decode-sized token counts: weights decoded straight into warp-MMA
+    # registers (one and two 8-token tiles; one, two and four 16-row groups
+    # per CTA; ragged N; long K)
+    x, w, bias, ref = _case(m, n, k, 23 + m + n, fmt, with_bias=with_bias)
+    ops.set_pair_mode(5)
+    try:
+        plan = ops.plan_info(m, n, k, 0 if fmt == "nf4" else 1)
+        assert plan["smallm"] and plan["splits"] == 1
+        y = _run(ops, fmt, x, w, bias, n)
+        y2 = _run(ops, fmt, x, w, bias, n)
+        torch.cuda.synchronize()
+    finally:
+        ops.set_pair_mode(0)
+    assert R.rel_err(to_bits(y), ref) <= TOL
+    assert torch.equal(y, y2)
 
 
 def test_leading_dims_and_noncontiguous_input(ops):
@@ -241,7 +270,8 @@ def test_golden_linear(ops):
                                                   (2, 192, 0, 300, 640, 512),   # fused pair
                                                   (3, 256, 0, 300, 640, 512),   # two-phase
                                                   (4, 256, 0, 300, 640, 512),   # two launches
-                                                  (1, 0, 3, 16, 640, 1088)])    # split-K reduce
+                                                  (1, 0, 3, 16, 640, 1088),     # split-K reduce
+                                                  (5, 0, 0, 12, 640, 1024)])    # small-M kernel
 def test_gelu_tanh_epilogue(ops, fmt, mode, bm, splits, m, n, k):
     # y = bf16(gelu_tanh(bf16(x W^T + b))) in the epilogue equals the linear
     # followed by torch's GELU-tanh on its bf16 output (the reference's
@@ -280,8 +310,15 @@ def test_plan_choice(ops):
     assert ops.workspace_size(4608, 12288, 3072) == 12288 * 3072 * 2 + 256
     mid = ops.plan_info(512, 12288, 3072)
     assert not mid["twophase"]
+    # decode-sized batches: the small-M kernel (one 8-token tile always, two
+    # only with two 16-row groups per CTA), else fused one-CTA tiles
+    assert ops.plan_info(1, 18432, 3072)["smallm"]
+    assert ops.plan_info(8, 3072, 3072)["bm"] == 8
+    assert ops.plan_info(16, 18432, 3072)["smallm"]
     small = ops.plan_info(16, 3072, 3072)
-    assert not small["pair"] and small["bm"] == 16 and small["splits"] > 1
+    assert not small["smallm"] and not small["pair"] and small["bm"] == 16 and small["splits"] > 1
+    assert not ops.plan_info(4, 3072, 3008)["smallm"]  # K % 128 != 0: fused kernel
+    assert ops.workspace_size(4, 3072, 3072) == 0
 
 
 def test_no_kernel_error_recorded(ops):
