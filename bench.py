@@ -53,7 +53,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["tp_fp8", "flux_dit"], default="nf4")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["tp_fp8", "flux_dit", "small_nf4", "small_fp8"],
+                    default="nf4")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
@@ -739,16 +740,169 @@ def run_flux(args, world, rank, local):
         dist.destroy_process_group()
 
 
+# ------------------------------------------------- decode-sized token counts
+SMALL_N, SMALL_K = 18432, 3072  # the FLUX AdaLN modulation projection (3072 -> 6 x 3072)
+SMALL_MS = (1, 16, 64, 512)
+SMALL_ROTATE = 8  # 8 weight copies (255 MB NF4) > 126 MB L2
+
+
+def run_small(args, world, rank, local):
+    """The small-M sweep: x[M, 3072] . W[18432, 3072]^T for M in 1, 16, 64,
+    512, each as a CUDA graph of 40 calls over 8 rotating weight copies.
+    M <= 64 is HBM-bound on the weight, so the value is GB/s at M = 1 against
+    the measured HBM copy bandwidth; every M is reported."""
+    from diffuser_b200 import modules, ops
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    fmt = args.workload.split("_")[1]
+    n, k = SMALL_N, SMALL_K
+    stream = torch.cuda.current_stream(dev)
+    g0 = torch.Generator(device=dev).manual_seed(0)
+    w = torch.randn(n, k, generator=g0, device=dev) * 0.02
+    if fmt == "nf4":
+        p0, a0 = ops.ltx23_nf4_quantize(w)
+        wsets = [(p0.clone(), a0.clone()) for _ in range(SMALL_ROTATE)]
+        wbytes = n * k // 2 + n * k // 64 * 4
+        call = lambda i, x: ops.nf4_linear(x, *wsets[i % SMALL_ROTATE], n)
+    else:
+        w80, s0 = ops.fp8_quantize(w)
+        scale = float(s0.item())
+        wsets = [w80.clone() for _ in range(SMALL_ROTATE)]
+        wbytes = n * k
+        call = lambda i, x: ops.fp8_linear(x, wsets[i % SMALL_ROTATE], scale)
+    del w
+    per_graph = 40
+    reps = max(1, args.steps // per_graph)
+    rows = []
+    with ClockSampler(local) as clk:
+        for m in SMALL_MS:
+            gx = torch.Generator(device=dev).manual_seed(1 + 100 * rank)
+            x = torch.randn(m, k, generator=gx, device=dev).to(torch.bfloat16)
+            for i in range(max(args.warmup, 3)):
+                call(i, x)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for i in range(per_graph):
+                    call(i, x)
+            graph.replay()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            barrier(world)
+            torch.cuda.synchronize()
+            a.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            b.record(stream)
+            torch.cuda.synchronize()
+            barrier(world)
+            us = max_over_ranks(a.elapsed_time(b) * 1e3 / (reps * per_graph), world, dev)
+            del graph
+            plan = ops.plan_info(m, n, k, 0 if fmt == "nf4" else 1)
+            byts = wbytes + m * k * 2 + m * n * 2
+            rows.append({"M": m, "us": us, "GB_per_s": byts / us / 1e3,
+                         "TFLOP_per_s": 2 * m * n * k / us / 1e6, "algorithmic_bytes": byts,
+                         "kernel": plan["kernel"], "tile_tokens": plan["bm"], "splits": plan["splits"]})
+    err = ops.device_error(dev)
+    if err != 0:
+        raise RuntimeError(f"kernel error word {err}")
+
+    # M = 1 end to end through the public module with host buffers: x up,
+    # y down, every call
+    mod = (modules.ltx23_nf4_linear(n, k, bias=False) if fmt == "nf4"
+           else modules.ltx23_fp8_linear(n, k, bias=False)).to(dev)
+    if fmt == "nf4":
+        mod.set_nf4_weight(*wsets[0])
+    else:
+        mod.set_fp8_weight(wsets[0].view(torch.float8_e4m3fn), torch.tensor(scale))
+    xh = torch.randn(1, k).to(torch.bfloat16).pin_memory()
+    yh = torch.empty(1, n, dtype=torch.bfloat16).pin_memory()
+    n_e2e = max(10, min(args.steps, 200))
+
+    def e2e_step():
+        y = mod(xh.to(dev, non_blocking=True))
+        yh.copy_(y, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(n_e2e):
+        e2e_step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    e_us = max_over_ranks(a.elapsed_time(b) * 1e3 / n_e2e, world, dev)
+
+    # the reference's GPU algorithm at M = 1: decode the whole weight, then cuBLAS
+    ref_us = None
+    if world == 1:
+        rdq = RefGpuDequant(dev)
+        x1 = torch.randn(1, k, device=dev).to(torch.bfloat16)
+
+        def ref_step(i):
+            wb = rdq.nf4(*wsets[i % SMALL_ROTATE], n, k) if fmt == "nf4" else rdq.fp8(wsets[i % SMALL_ROTATE].view(torch.uint8), scale)
+            return torch.nn.functional.linear(x1, wb)
+        for i in range(3):
+            ref_step(i)
+        torch.cuda.synchronize()
+        a.record(stream)
+        for i in range(20):
+            ref_step(i)
+        b.record(stream)
+        torch.cuda.synchronize()
+        ref_us = a.elapsed_time(b) * 1e3 / 20
+        del rdq
+
+    if rank == 0:
+        _, _, hbm, peak_src = measured_peaks()
+        r1 = rows[0]
+        line = {
+            "metric": f"{fmt.upper()} small-M quant-linear GB/s (M=1, {k}->{n})",
+            "value": world * r1["GB_per_s"], "unit": "GB/s", "n_gpus": world,
+            "steps": reps * per_graph, "warmup": max(args.warmup, 3), "ms_per_step": r1["us"] / 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": f"{fmt}_linear x[M,{k}]bf16 . W[{n},{k}]{fmt}^T, M in {list(SMALL_MS)}",
+                       "parallelism": f"dp{world} (replicas, no collective)",
+                       "l2": f"{SMALL_ROTATE} rotating weight copies ({SMALL_ROTATE * wbytes / 1e6:.0f} MB) > 126 MB L2",
+                       "launch": "CUDA graph of 40 calls"},
+            "roofline": {"bound": "hbm", "achieved": r1["GB_per_s"], "peak": hbm, "unit": "GB/s",
+                         "frac": r1["GB_per_s"] / hbm, "traffic": None,
+                         "peak_source": f"{peak_src} HBM copy bandwidth",
+                         "kernel": r1["kernel"], "algorithmic_bytes": r1["algorithmic_bytes"]},
+            "sweep": rows,
+            "reference_gpu_algorithm_us_M1": ref_us,
+            "speedup_vs_reference_gpu_algorithm_M1": (ref_us / r1["us"]) if ref_us else None,
+            "cpu_baseline": None,
+            "e2e": {"value": world * r1["algorithmic_bytes"] / e_us / 1e3, "unit": "GB/s",
+                    "h2d_bytes_per_step": k * 2, "d2h_bytes_per_step": n * 2, "us_per_step": e_us,
+                    "api": f"diffuser_b200.modules.ltx23_{fmt}_linear.forward (eager, one call per step)"},
+            "gpu_launches": reps * per_graph,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
-        if args.workload in ("tp_fp8", "flux_dit"):
+        if args.workload in ("tp_fp8", "flux_dit", "small_nf4", "small_fp8"):
             if rank == 0:
                 why = ("the reference runs each linear on one GPU; it has no column-parallel path"
                        if args.workload == "tp_fp8" else
                        "the reference's FLUX step runs in R (not installed); its GPU linear algorithm "
-                       "is timed inside the flux_dit line (reference_algorithm_step_ms)")
+                       "is timed inside the flux_dit line (reference_algorithm_step_ms)"
+                       if args.workload == "flux_dit" else
+                       "the small-M sweep times the reference's GPU algorithm at M = 1 inside its own line "
+                       "(reference_gpu_algorithm_us_M1); the CPU reference arm runs on the default workload")
                 print(json.dumps({"impl": "reference", "unavailable": why}))
             return
         run_reference_arm(args, world, rank)
@@ -758,6 +912,9 @@ def main():
         return
     if args.workload == "flux_dit":
         run_flux(args, world, rank, local)
+        return
+    if args.workload.startswith("small_"):
+        run_small(args, world, rank, local)
         return
     run_ours(args, world, rank, local)
 
