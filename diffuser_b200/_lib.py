@@ -53,6 +53,12 @@ SIGNATURES = {
     "dq_heads_to_tokens": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                           ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
                                           ctypes.c_void_p]),
+    "dq_adaln_modulate": (ctypes.c_int, [ctypes.c_void_p, _c_i64, _c_i64, ctypes.c_int, ctypes.c_int,
+                                         ctypes.c_void_p, ctypes.c_void_p, _c_i64, ctypes.c_float,
+                                         ctypes.c_void_p, _c_i64, ctypes.c_void_p]),
+    "dq_gated_residual": (ctypes.c_int, [ctypes.c_void_p, _c_i64, ctypes.c_void_p, _c_i64, ctypes.c_void_p,
+                                         _c_i64, _c_i64, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, _c_i64,
+                                         ctypes.c_void_p]),
     "dq_linear_nf4_ex": (ctypes.c_int, [ctypes.c_void_p, _c_i64, _c_i64, ctypes.c_void_p, ctypes.c_void_p,
                                         ctypes.c_void_p, _c_i64, ctypes.c_int, ctypes.c_void_p,
                                         ctypes.c_void_p, _c_sz, ctypes.c_void_p]),

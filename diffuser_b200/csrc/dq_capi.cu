@@ -838,6 +838,16 @@ static int tp_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8_t* 
 
 using namespace dq;
 
+template <int NPT>
+static void launch_adaln(const void* x, int64_t ld_x, int64_t T, int S, int D, const void* scale,
+                         const void* shift, int64_t ld_mod, float eps, void* out, int64_t ld_out,
+                         cudaStream_t st) {
+  adaln_modulate_kernel<NPT><<<static_cast<int>(T), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(x), ld_x, S, D, static_cast<const __nv_bfloat16*>(scale),
+      static_cast<const __nv_bfloat16*>(shift), ld_mod, eps, static_cast<__nv_bfloat16*>(out),
+      ld_out);
+}
+
 extern "C" {
 
 const char* dq_version(void) { return DQ_VERSION_STRING; }
@@ -1108,33 +1118,27 @@ int dq_qk_norm_rope(const void* img, int64_t ld_img, const void* txt, int64_t ld
   if (S_txt > 0 && (w_img == nullptr) != (w_txt == nullptr)) return DQ_ERR_ARG;
   if (ld_img < static_cast<int64_t>(H) * D || (S_txt > 0 && ld_txt < static_cast<int64_t>(H) * D))
     return DQ_ERR_SHAPE;
-  const int64_t warps = static_cast<int64_t>(B) * (S_img + S_txt) * H;
-  if (warps == 0) return DQ_OK;
-  const int64_t blocks = (warps * 32 + 255) / 256;
+  // one CTA per token, up to 16 warps looping over the heads
+  const int64_t blocks = static_cast<int64_t>(B) * (S_img + S_txt);
+  if (blocks == 0) return DQ_OK;
   if (blocks > INT32_MAX) return DQ_ERR_SHAPE;
+  const int threads = 32 * std::min(H, 16);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto bf = [](const void* p) { return static_cast<const __nv_bfloat16*>(p); };
+  // wide accesses when every row start is 16-byte aligned
+  const bool vec = aligned(img, 16) && aligned(txt, 16) && aligned(out, 16) && aligned(w_img, 16) &&
+                   aligned(w_txt, 16) && aligned(cos_t, 16) && aligned(sin_t, 16) &&
+                   ld_img % 8 == 0 && (S_txt == 0 || ld_txt % 8 == 0);
+  auto launch = [&](auto kern) {
+    kern<<<static_cast<int>(blocks), threads, 0, st>>>(bf(img), ld_img, bf(txt), ld_txt, B, S_img, S_txt,
+                                                   H, bf(w_img), bf(w_txt), cos_t, sin_t, eps,
+                                                   static_cast<__nv_bfloat16*>(out));
+  };
   switch (D / 32) {
-    case 2:
-      qk_norm_rope_kernel<2><<<static_cast<int>(blocks), 256, 0, st>>>(
-          bf(img), ld_img, bf(txt), ld_txt, B, S_img, S_txt, H, bf(w_img), bf(w_txt), cos_t, sin_t,
-          eps, static_cast<__nv_bfloat16*>(out));
-      break;
-    case 4:
-      qk_norm_rope_kernel<4><<<static_cast<int>(blocks), 256, 0, st>>>(
-          bf(img), ld_img, bf(txt), ld_txt, B, S_img, S_txt, H, bf(w_img), bf(w_txt), cos_t, sin_t,
-          eps, static_cast<__nv_bfloat16*>(out));
-      break;
-    case 6:
-      qk_norm_rope_kernel<6><<<static_cast<int>(blocks), 256, 0, st>>>(
-          bf(img), ld_img, bf(txt), ld_txt, B, S_img, S_txt, H, bf(w_img), bf(w_txt), cos_t, sin_t,
-          eps, static_cast<__nv_bfloat16*>(out));
-      break;
-    case 8:
-      qk_norm_rope_kernel<8><<<static_cast<int>(blocks), 256, 0, st>>>(
-          bf(img), ld_img, bf(txt), ld_txt, B, S_img, S_txt, H, bf(w_img), bf(w_txt), cos_t, sin_t,
-          eps, static_cast<__nv_bfloat16*>(out));
-      break;
+    case 2: vec ? launch(qk_norm_rope_kernel<2, true>) : launch(qk_norm_rope_kernel<2, false>); break;
+    case 4: vec ? launch(qk_norm_rope_kernel<4, true>) : launch(qk_norm_rope_kernel<4, false>); break;
+    case 6: vec ? launch(qk_norm_rope_kernel<6, true>) : launch(qk_norm_rope_kernel<6, false>); break;
+    case 8: vec ? launch(qk_norm_rope_kernel<8, true>) : launch(qk_norm_rope_kernel<8, false>); break;
     default:
       return DQ_ERR_SHAPE;
   }
@@ -1146,21 +1150,66 @@ int dq_heads_to_tokens(const void* in, int B, int H, int S_txt, int S_img, int D
   if (B <= 0 || H <= 0 || S_txt < 0 || S_img < 0 || D <= 0 || D % 64 != 0 || D > 256)
     return DQ_ERR_SHAPE;
   if (in == nullptr || out_img == nullptr || (S_txt > 0 && out_txt == nullptr)) return DQ_ERR_ARG;
-  const int64_t warps = static_cast<int64_t>(B) * (S_img + S_txt) * H;
-  if (warps == 0) return DQ_OK;
-  const int64_t blocks = (warps * 32 + 255) / 256;
+  const int64_t blocks = static_cast<int64_t>(B) * (S_img + S_txt);
+  if (blocks == 0) return DQ_OK;
   if (blocks > INT32_MAX) return DQ_ERR_SHAPE;
+  const int threads = 32 * std::min(H, 16);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(in);
   __nv_bfloat16* ot = static_cast<__nv_bfloat16*>(out_txt);
   __nv_bfloat16* oi = static_cast<__nv_bfloat16*>(out_img);
+  const bool vec = aligned(in, 16) && aligned(out_txt, 16) && aligned(out_img, 16);
+  auto launch = [&](auto kern) {
+    kern<<<static_cast<int>(blocks), threads, 0, st>>>(src, B, H, S_txt, S_img, ot, oi);
+  };
   switch (D / 32) {
-    case 2: heads_to_tokens_kernel<2><<<static_cast<int>(blocks), 256, 0, st>>>(src, B, H, S_txt, S_img, ot, oi); break;
-    case 4: heads_to_tokens_kernel<4><<<static_cast<int>(blocks), 256, 0, st>>>(src, B, H, S_txt, S_img, ot, oi); break;
-    case 6: heads_to_tokens_kernel<6><<<static_cast<int>(blocks), 256, 0, st>>>(src, B, H, S_txt, S_img, ot, oi); break;
-    case 8: heads_to_tokens_kernel<8><<<static_cast<int>(blocks), 256, 0, st>>>(src, B, H, S_txt, S_img, ot, oi); break;
+    case 2: vec ? launch(heads_to_tokens_kernel<2, true>) : launch(heads_to_tokens_kernel<2, false>); break;
+    case 4: vec ? launch(heads_to_tokens_kernel<4, true>) : launch(heads_to_tokens_kernel<4, false>); break;
+    case 6: vec ? launch(heads_to_tokens_kernel<6, true>) : launch(heads_to_tokens_kernel<6, false>); break;
+    case 8: vec ? launch(heads_to_tokens_kernel<8, true>) : launch(heads_to_tokens_kernel<8, false>); break;
     default: return DQ_ERR_SHAPE;
   }
+  return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
+}
+
+int dq_adaln_modulate(const void* x, int64_t ld_x, int64_t T, int S, int D, const void* scale,
+                      const void* shift, int64_t ld_mod, float eps, void* out, int64_t ld_out,
+                      dq_stream_t stream) {
+  if (T < 0 || S <= 0 || D <= 0 || D % 4 != 0 || D > 8192 || T % S != 0 || T > INT32_MAX)
+    return DQ_ERR_SHAPE;
+  if (T == 0) return DQ_OK;
+  if (x == nullptr || scale == nullptr || shift == nullptr || out == nullptr) return DQ_ERR_ARG;
+  if (ld_x < D || ld_mod < D || ld_out < D || ld_x % 4 || ld_mod % 4 || ld_out % 4) return DQ_ERR_SHAPE;
+  if (!aligned(x, 8) || !aligned(scale, 8) || !aligned(shift, 8) || !aligned(out, 8))
+    return DQ_ERR_ALIGN;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int runs = (D / 4 + 255) / 256;  // 4-feature runs per thread
+  if (runs <= 2)
+    launch_adaln<2>(x, ld_x, T, S, D, scale, shift, ld_mod, eps, out, ld_out, st);
+  else if (runs <= 4)
+    launch_adaln<4>(x, ld_x, T, S, D, scale, shift, ld_mod, eps, out, ld_out, st);
+  else
+    launch_adaln<8>(x, ld_x, T, S, D, scale, shift, ld_mod, eps, out, ld_out, st);
+  return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
+}
+
+int dq_gated_residual(const void* x, int64_t ld_x, const void* gate, int64_t ld_mod, const void* y,
+                      int64_t ld_y, int64_t T, int S, int D, void* out, int64_t ld_out,
+                      dq_stream_t stream) {
+  if (T < 0 || S <= 0 || D <= 0 || D % 4 != 0 || T % S != 0) return DQ_ERR_SHAPE;
+  if (T == 0) return DQ_OK;
+  if (x == nullptr || gate == nullptr || y == nullptr || out == nullptr) return DQ_ERR_ARG;
+  if (ld_x < D || ld_mod < D || ld_y < D || ld_out < D || ld_x % 4 || ld_mod % 4 || ld_y % 4 ||
+      ld_out % 4)
+    return DQ_ERR_SHAPE;
+  if (!aligned(x, 8) || !aligned(gate, 8) || !aligned(y, 8) || !aligned(out, 8)) return DQ_ERR_ALIGN;
+  DeviceInfo* d = nullptr;
+  const int rc = current_device(&d);
+  if (rc != DQ_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  gated_residual_kernel<<<grid_for(T * (D / 4), 256, d->sms), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(x), ld_x, static_cast<const __nv_bfloat16*>(gate), ld_mod,
+      static_cast<const __nv_bfloat16*>(y), ld_y, T, S, D, static_cast<__nv_bfloat16*>(out), ld_out);
   return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
 }
 

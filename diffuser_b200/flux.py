@@ -68,6 +68,69 @@ def heads_to_tokens(x, s_txt: int):
     return txt, img
 
 
+# AdaLN modulation and gated residuals as one kernel each (False: the
+# reference's chain of tensor ops).
+FUSED_ADALN = True
+
+
+def _rows(t):
+    """(tensor, row stride) with unit stride along the last dim and rows of a
+    [B, S, D] tensor evenly spaced; copies only when they are not."""
+    if t.stride(-1) != 1 or (t.dim() == 3 and t.stride(0) != t.shape[1] * t.stride(1)):
+        t = t.contiguous()
+    return t, t.stride(-2)
+
+
+def adaln_modulate(x, scale, shift, eps: float = 1e-6):
+    """LayerNorm(x) * (1 + scale[:, None]) + shift[:, None] for x [B, S, D]
+    bf16, scale / shift [B, D], rounded to bf16 after each op like the tensor
+    chain (R/dit_flux_modules.R:26-42), in one kernel."""
+    b, s, d = x.shape
+    x, ldx = _rows(x)
+    scale, ldm = _rows(scale)
+    shift, ldm2 = _rows(shift)
+    if ldm2 != ldm:
+        scale, shift = scale.contiguous(), shift.contiguous()
+        ldm = d
+    out = torch.empty((b, s, d), dtype=torch.bfloat16, device=x.device)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
+    rc = _lib.lib().dq_adaln_modulate(_ptr(x), ldx, b * s, s, d, _ptr(scale), _ptr(shift), ldm,
+                                      ctypes.c_float(eps), _ptr(out), d, stream)
+    _lib.check("dq_adaln_modulate", rc)
+    return out
+
+
+def gated_residual(x, gate, y):
+    """x + gate[:, None] * y for x, y [B, S, D] bf16 and gate [B, D], rounded
+    like the two tensor ops, in one kernel."""
+    b, s, d = x.shape
+    x, ldx = _rows(x)
+    y, ldy = _rows(y)
+    gate, ldm = _rows(gate)
+    out = torch.empty((b, s, d), dtype=torch.bfloat16, device=x.device)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
+    rc = _lib.lib().dq_gated_residual(_ptr(x), ldx, _ptr(gate), ldm, _ptr(y), ldy, b * s, s, d,
+                                      _ptr(out), d, stream)
+    _lib.check("dq_gated_residual", rc)
+    return out
+
+
+def _adaln_ok(x):
+    return FUSED_ADALN and x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 3 and x.shape[-1] % 4 == 0
+
+
+def _modulate(norm, x, scale, shift):
+    if _adaln_ok(x) and norm.weight is None and norm.bias is None:
+        return adaln_modulate(x, scale, shift, norm.eps)
+    return norm(x) * (scale[:, None] + 1) + shift[:, None]
+
+
+def _gated_add(x, gate, y):
+    if _adaln_ok(x) and y.shape == x.shape:
+        return gated_residual(x, gate, y)
+    return x + gate[:, None] * y
+
+
 # GELU-tanh after the up-projections runs in the quantized linear's epilogue
 # (False: a separate activation pass, as the reference does).
 FUSED_GELU = True
@@ -170,7 +233,7 @@ class AdaLayerNormZero(nn.Module):
 
     def forward(self, x, emb):
         p = self.linear(F.silu(emb)).chunk(6, dim=1)
-        x = self.norm(x) * (p[1][:, None] + 1) + p[0][:, None]
+        x = _modulate(self.norm, x, p[1], p[0])
         return x, p[2], p[3], p[4], p[5]
 
 
@@ -184,7 +247,7 @@ class AdaLayerNormZeroSingle(nn.Module):
 
     def forward(self, x, emb):
         p = self.linear(F.silu(emb)).chunk(3, dim=1)
-        return self.norm(x) * (p[1][:, None] + 1) + p[0][:, None], p[2]
+        return _modulate(self.norm, x, p[1], p[0]), p[2]
 
 
 class AdaLayerNormContinuous(nn.Module):
@@ -328,11 +391,11 @@ class DoubleBlock(nn.Module):
         nx, g_msa, sh_mlp, sc_mlp, g_mlp = self.norm1(x, temb)
         nc, cg_msa, csh_mlp, csc_mlp, cg_mlp = self.norm1_context(ctx, temb)
         a_img, a_txt = self.attn(nx, nc, rope)
-        x = x + g_msa[:, None] * a_img
-        x = x + g_mlp[:, None] * self.ff(self.norm2(x) * (sc_mlp[:, None] + 1) + sh_mlp[:, None])
-        ctx = ctx + cg_msa[:, None] * a_txt
-        ctx = ctx + cg_mlp[:, None] * self.ff_context(
-            self.norm2_context(ctx) * (csc_mlp[:, None] + 1) + csh_mlp[:, None])
+        x = _gated_add(x, g_msa, a_img)
+        x = _gated_add(x, g_mlp, self.ff(_modulate(self.norm2, x, sc_mlp, sh_mlp)))
+        ctx = _gated_add(ctx, cg_msa, a_txt)
+        ctx = _gated_add(ctx, cg_mlp, self.ff_context(
+            _modulate(self.norm2_context, ctx, csc_mlp, csh_mlp)))
         if ctx.dtype == torch.float16:
             ctx = ctx.clamp(-65504, 65504)
         return ctx, x
@@ -353,7 +416,7 @@ class SingleBlock(nn.Module):
         n, gate = self.norm(x, temb)
         mlp = _proj_gelu_tanh(self.proj_mlp, n)
         a = self.attn(n, rope=rope)
-        x = x + gate[:, None] * self.proj_out(torch.cat([a, mlp], dim=2))
+        x = _gated_add(x, gate, self.proj_out(torch.cat([a, mlp], dim=2)))
         if x.dtype == torch.float16:
             x = x.clamp(-65504, 65504)
         return x

@@ -5,8 +5,9 @@
  * reference's tensor ops around the attention (R/dit_flux_modules.R:161-212:
  * per-head ltx23_rms_norm, the [text; image] concatenation, the transpose to
  * head-major, flux_apply_rotary_emb R/rope_flux.R:96-110, and the way back).
- * bf16 tensors, device pointers, the given stream; D (the head dimension) a
- * multiple of 64 up to 256. */
+ * bf16 tensors, device pointers, the given stream; for the attention glue D
+ * (the head dimension) is a multiple of 64 up to 256.  The AdaLN glue below
+ * fuses the modulation and gated-residual tensor ops around the blocks. */
 #ifndef DQ_DIT_H
 #define DQ_DIT_H
 
@@ -31,6 +32,23 @@ int dq_qk_norm_rope(const void* img, int64_t ld_img, const void* txt, int64_t ld
  * out_img [B, S_img, H*D]. */
 int dq_heads_to_tokens(const void* in, int B, int H, int S_txt, int S_img, int D, void* out_txt,
                        void* out_img, dq_stream_t stream);
+
+/* AdaLN-Zero modulation (R/dit_flux_modules.R:26-42 and 54-70; the norm2
+ * lines of flux_double_block): x [T, D] (row stride ld_x, T = B * S tokens,
+ * batch element t / S) -> out = bf16(bf16(bf16(LayerNorm(x)) * bf16(1 +
+ * scale)) + shift), LayerNorm without affine with eps, statistics in float32;
+ * scale / shift [B, D] rows with row stride ld_mod.  D a multiple of 4 up to
+ * 8192; every row start 8-byte aligned. */
+int dq_adaln_modulate(const void* x, int64_t ld_x, int64_t T, int S, int D, const void* scale,
+                      const void* shift, int64_t ld_mod, float eps, void* out, int64_t ld_out,
+                      dq_stream_t stream);
+
+/* Gated residual of the same blocks: out = bf16(x + bf16(gate * y)), gate
+ * [B, D] (row stride ld_mod) broadcast over each batch element's S tokens;
+ * out may be x.  D a multiple of 4; every row start 8-byte aligned. */
+int dq_gated_residual(const void* x, int64_t ld_x, const void* gate, int64_t ld_mod, const void* y,
+                      int64_t ld_y, int64_t T, int S, int D, void* out, int64_t ld_out,
+                      dq_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -95,6 +95,68 @@ def test_flux_step_captures_in_a_cuda_graph():
     assert torch.equal(out, eager)
 
 
+def test_fused_attention_glue_wide_and_scalar_accesses_agree():
+    # the kernels move aligned rows with 16/8/4-byte accesses and fall back to
+    # element accesses for unaligned views (odd row stride or offset): both
+    # give the same bits
+    from diffuser_b200 import flux
+    torch.manual_seed(1)
+    dev = torch.device("cuda", 0)
+    for (B, S_img, S_txt, H, D) in ((2, 21, 5, 3, 128), (1, 9, 4, 2, 64), (1, 7, 2, 2, 192),
+                                    (1, 6, 3, 1, 256)):
+        wide_i = torch.randn(B, S_img, H * D + 1, device=dev).to(torch.bfloat16)
+        wide_t = torch.randn(B, S_txt, H * D + 1, device=dev).to(torch.bfloat16)
+        img_u, txt_u = wide_i[..., 1:], wide_t[..., 1:]          # unaligned views
+        img_a, txt_a = img_u.contiguous(), txt_u.contiguous()    # aligned copies
+        w_img = (1 + 0.1 * torch.randn(D, device=dev)).to(torch.bfloat16)
+        w_txt = (1 + 0.1 * torch.randn(D, device=dev)).to(torch.bfloat16)
+        pos = torch.randint(0, 64, (S_txt + S_img, 3), device=dev).float()
+        axes = {64: (16, 24, 24), 128: (16, 56, 56), 192: (32, 80, 80), 256: (32, 112, 112)}[D]
+        rope = flux.pos_embed(pos, axes)
+        with torch.no_grad():
+            a = flux.qk_norm_rope(img_a, txt_a, H, w_img, w_txt, rope)
+            u = flux.qk_norm_rope(img_u, txt_u, H, w_img, w_txt, rope)
+            assert torch.equal(a, u)
+            assert torch.equal(flux.qk_norm_rope(img_a, txt_a, H), flux.qk_norm_rope(img_u, txt_u, H))
+            t_out, i_out = flux.heads_to_tokens(a, S_txt)
+            # an unaligned source for the inverse layout: offset by one element
+            buf = torch.empty(a.numel() + 1, dtype=torch.bfloat16, device=dev)
+            a_u = buf[1:].view(a.shape)
+            a_u.copy_(a)
+            t_u, i_u = flux.heads_to_tokens(a_u, S_txt)
+            assert torch.equal(t_out, t_u) and torch.equal(i_out, i_u)
+
+
+def test_adaln_glue_matches_tensor_ops():
+    # AdaLN modulation and gated residual kernels vs the blocks' tensor-op
+    # chains (R/dit_flux_modules.R:26-42, 54-70, 280-321): the residual is
+    # the same bits; the modulation's LayerNorm statistics are summed in
+    # another order, so its normalized value can sit one bf16 step away
+    from diffuser_b200 import flux
+    torch.manual_seed(2)
+    dev = torch.device("cuda", 0)
+    for (B, S, D) in ((2, 37, 256), (1, 65, 3072), (3, 5, 1028), (1, 3, 8192)):
+        x = (torch.randn(B, S, D, device=dev) * 3 + 0.5).to(torch.bfloat16)
+        mods = (torch.randn(B, 6 * D, device=dev) * 0.5).to(torch.bfloat16)
+        p = mods.chunk(6, dim=1)                                  # strided [B, D] views
+        norm = torch.nn.LayerNorm(D, eps=1e-6, elementwise_affine=False)
+        with torch.no_grad():
+            ref = norm(x) * (p[1][:, None] + 1) + p[0][:, None]
+            got = flux.adaln_modulate(x, p[1], p[0], 1e-6)
+            assert got.shape == ref.shape and got.dtype == torch.bfloat16
+            # one bf16 step of the normalized value, carried through the scale
+            n = norm(x).float()
+            tol = (n.abs() * 2.0 ** -7 + 1e-6) * (p[1][:, None].float() + 1).abs() \
+                + ref.float().abs() * 2.0 ** -7
+            assert ((got.float() - ref.float()).abs() <= tol + 1e-6).all()
+            assert (got != ref).float().mean().item() < 0.02
+            y = torch.randn(B, S, D, device=dev).to(torch.bfloat16)
+            assert torch.equal(flux.gated_residual(x, p[2], y), x + p[2][:, None] * y)
+            # a non-contiguous y (every other token row)
+            y2 = torch.randn(B, 2 * S, D, device=dev).to(torch.bfloat16)[:, ::2]
+            assert torch.equal(flux.gated_residual(x, p[5], y2), x + p[5][:, None] * y2)
+
+
 def test_fused_attention_glue_matches_tensor_ops():
     # one kernel for norm + [text; image] + transpose + rotary vs the tensor-op
     # chain of the harness (R/dit_flux_modules.R:161-190, R/rope_flux.R:96-110)
