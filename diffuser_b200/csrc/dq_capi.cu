@@ -1118,11 +1118,11 @@ int dq_qk_norm_rope(const void* img, int64_t ld_img, const void* txt, int64_t ld
   if (S_txt > 0 && (w_img == nullptr) != (w_txt == nullptr)) return DQ_ERR_ARG;
   if (ld_img < static_cast<int64_t>(H) * D || (S_txt > 0 && ld_txt < static_cast<int64_t>(H) * D))
     return DQ_ERR_SHAPE;
-  // one CTA per token, up to 16 warps looping over the heads
+  // one CTA per token, a warp per kHeadsPerWarp heads (up to 16 warps)
   const int64_t blocks = static_cast<int64_t>(B) * (S_img + S_txt);
   if (blocks == 0) return DQ_OK;
   if (blocks > INT32_MAX) return DQ_ERR_SHAPE;
-  const int threads = 32 * std::min(H, 16);
+  const int threads = 32 * std::min((H + kHeadsPerWarp - 1) / kHeadsPerWarp, 16);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto bf = [](const void* p) { return static_cast<const __nv_bfloat16*>(p); };
   // wide accesses when every row start is 16-byte aligned
@@ -1153,7 +1153,7 @@ int dq_heads_to_tokens(const void* in, int B, int H, int S_txt, int S_img, int D
   const int64_t blocks = static_cast<int64_t>(B) * (S_img + S_txt);
   if (blocks == 0) return DQ_OK;
   if (blocks > INT32_MAX) return DQ_ERR_SHAPE;
-  const int threads = 32 * std::min(H, 16);
+  const int threads = 32 * std::min((H + kHeadsPerWarp - 1) / kHeadsPerWarp, 16);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(in);
   __nv_bfloat16* ot = static_cast<__nv_bfloat16*>(out_txt);

@@ -101,9 +101,12 @@ __device__ __forceinline__ void load_f32_run(const float* p, float* v) {
   }
 }
 
-// One CTA per token (b, s) of the [text; image] sequence, its warps looping
-// over the heads: the token's cos / sin slice is loaded once per warp, and
-// the only index arithmetic is one division per thread.
+// One CTA per token (b, s) of the [text; image] sequence; warp w owns heads
+// w*HPW .. w*HPW+HPW-1 (then the next round of nwarps*HPW heads) and issues
+// all their loads before computing, so HPW vectors per warp are in flight.
+// The token's cos / sin slice is loaded once per warp.
+constexpr int kHeadsPerWarp = 4;
+
 template <int EPL, bool VEC>
 __global__ void __launch_bounds__(512)
     qk_norm_rope_kernel(const __nv_bfloat16* __restrict__ img, int64_t ld_img,
@@ -112,6 +115,7 @@ __global__ void __launch_bounds__(512)
                         const __nv_bfloat16* __restrict__ w_txt, const float* __restrict__ cos_t,
                         const float* __restrict__ sin_t, float eps, __nv_bfloat16* __restrict__ out) {
   constexpr int D = EPL * 32;
+  constexpr int HPW = kHeadsPerWarp;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int nwarps = blockDim.x >> 5;
@@ -128,44 +132,52 @@ __global__ void __launch_bounds__(512)
     load_f32_run<EPL, VEC>(cos_t + static_cast<int64_t>(s) * D + EPL * lane, c);
     load_f32_run<EPL, VEC>(sin_t + static_cast<int64_t>(s) * D + EPL * lane, sn);
   }
-  for (int h = warp; h < H; h += nwarps) {
-    float x[EPL];
-    load_bf16_run<EPL, VEC>(row + static_cast<int64_t>(h) * D + EPL * lane, x);
-    if (w != nullptr) {
-      float ss = 0.f;
+  for (int h0 = warp * HPW; h0 < H; h0 += nwarps * HPW) {
+    float x[HPW][EPL];
 #pragma unroll
-      for (int i = 0; i < EPL; ++i) ss += x[i] * x[i];
+    for (int j = 0; j < HPW; ++j)
+      if (h0 + j < H) load_bf16_run<EPL, VEC>(row + static_cast<int64_t>(h0 + j) * D + EPL * lane, x[j]);
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      const float r = rsqrtf(ss / static_cast<float>(D) + eps);
+    for (int j = 0; j < HPW; ++j) {
+      const int h = h0 + j;
+      if (h >= H) break;  // warp-uniform
+      if (w != nullptr) {
+        float ss = 0.f;
 #pragma unroll
-      for (int i = 0; i < EPL; ++i) {
-        const float n = __bfloat162float(__float2bfloat16_rn(x[i] * r));
-        x[i] = __bfloat162float(__float2bfloat16_rn(n * wv[i]));
+        for (int i = 0; i < EPL; ++i) ss += x[j][i] * x[j][i];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float r = rsqrtf(ss / static_cast<float>(D) + eps);
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) {
+          const float n = __bfloat162float(__float2bfloat16_rn(x[j][i] * r));
+          x[j][i] = __bfloat162float(__float2bfloat16_rn(n * wv[i]));
+        }
       }
-    }
-    __nv_bfloat16* dst = out + ((static_cast<int64_t>(b) * H + h) * S + s) * D + EPL * lane;
-    if (cos_t != nullptr) {
-      float o[EPL];
+      __nv_bfloat16* dst = out + ((static_cast<int64_t>(b) * H + h) * S + s) * D + EPL * lane;
+      if (cos_t != nullptr) {
+        float o[EPL];
 #pragma unroll
-      for (int i = 0; i < EPL; i += 2) {
-        // rotated pair: (-x[i+1], x[i])
-        o[i] = __fadd_rn(__fmul_rn(x[i], c[i]), __fmul_rn(-x[i + 1], sn[i]));
-        o[i + 1] = __fadd_rn(__fmul_rn(x[i + 1], c[i + 1]), __fmul_rn(x[i], sn[i + 1]));
+        for (int i = 0; i < EPL; i += 2) {
+          // rotated pair: (-x[i+1], x[i])
+          o[i] = __fadd_rn(__fmul_rn(x[j][i], c[i]), __fmul_rn(-x[j][i + 1], sn[i]));
+          o[i + 1] = __fadd_rn(__fmul_rn(x[j][i + 1], c[i + 1]), __fmul_rn(x[j][i], sn[i + 1]));
+        }
+        store_bf16_run<EPL, VEC>(dst, o);
+      } else {
+        store_bf16_run<EPL, VEC>(dst, x[j]);
       }
-      store_bf16_run<EPL, VEC>(dst, o);
-    } else {
-      store_bf16_run<EPL, VEC>(dst, x);
     }
   }
 }
 
-// One CTA per token, warps over heads (as above).
+// One CTA per token, warps over groups of HPW heads (as above).
 template <int EPL, bool VEC>
 __global__ void __launch_bounds__(512)
     heads_to_tokens_kernel(const __nv_bfloat16* __restrict__ in, int B, int H, int S_txt, int S_img,
                            __nv_bfloat16* __restrict__ out_txt, __nv_bfloat16* __restrict__ out_img) {
   constexpr int D = EPL * 32;
+  constexpr int HPW = kHeadsPerWarp;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int nwarps = blockDim.x >> 5;
@@ -175,24 +187,18 @@ __global__ void __launch_bounds__(512)
   __nv_bfloat16* drow =
       s < S_txt ? out_txt + (static_cast<int64_t>(b) * S_txt + s) * H * D
                 : out_img + (static_cast<int64_t>(b) * S_img + (s - S_txt)) * H * D;
-  for (int h = warp; h < H; h += nwarps) {
-    const __nv_bfloat16* src = in + ((static_cast<int64_t>(b) * H + h) * S + s) * D + EPL * lane;
-    __nv_bfloat16* dst = drow + static_cast<int64_t>(h) * D + EPL * lane;
-    if constexpr (VEC) {
-      // a plain copy: the bf16 run as 32-bit words, widest aligned access
-      constexpr int W = EPL % 8 == 0 ? 4 : EPL % 4 == 0 ? 2 : 1;
+  for (int h0 = warp * HPW; h0 < H; h0 += nwarps * HPW) {
+    float v[HPW][EPL];
 #pragma unroll
-      for (int i = 0; i < EPL / (2 * W); ++i) {
-        if constexpr (W == 4)
-          reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
-        else if constexpr (W == 2)
-          reinterpret_cast<uint2*>(dst)[i] = reinterpret_cast<const uint2*>(src)[i];
-        else
-          reinterpret_cast<uint32_t*>(dst)[i] = reinterpret_cast<const uint32_t*>(src)[i];
-      }
-    } else {
+    for (int j = 0; j < HPW; ++j)
+      if (h0 + j < H)
+        load_bf16_run<EPL, VEC>(in + ((static_cast<int64_t>(b) * H + h0 + j) * S + s) * D + EPL * lane,
+                                v[j]);
 #pragma unroll
-      for (int i = 0; i < EPL; ++i) dst[i] = src[i];
+    for (int j = 0; j < HPW; ++j) {
+      if (h0 + j >= H) break;
+      // bf16 -> float -> bf16 is exact: a plain copy
+      store_bf16_run<EPL, VEC>(drow + static_cast<int64_t>(h0 + j) * D + EPL * lane, v[j]);
     }
   }
 }
