@@ -268,9 +268,11 @@ constexpr int64_t kSmallMMaxM = 16;
 // Row groups (16 weight rows each) per small-M CTA, so one CTA's LUT fill and
 // x loads serve more rows and more weight bytes are in flight per warp: the
 // most that still give every SM a CTA (measured: four for NF4 with one token
-// tile, two for fp8 and for two token tiles, whose registers run out).
+// tile when that still leaves about two CTAs per SM -- 3072->18432 12.7 us
+// against 16.9 with two, 4096->12288 15.9 against 14.2 -- two for fp8 and for
+// two token tiles, whose registers run out).
 static int smallm_r16(int fmt, int64_t M, int64_t N, int sms) {
-  if (fmt == kFmtNF4 && M <= 8 && (N + 63) / 64 >= sms) return 4;
+  if (fmt == kFmtNF4 && M <= 8 && 2 * ((N + 63) / 64) >= 3 * static_cast<int64_t>(sms)) return 4;
   return (N + 31) / 32 >= sms ? 2 : 1;
 }
 // Token count from which the two-phase plan is chosen: decoding the weight

@@ -59,6 +59,9 @@ struct SmallMCfg {
   static constexpr int kThreads = kWarps * 32;
   static constexpr int kRows = 16 * R16;
   static constexpr bool kPrefetch = R16 == 1;
+  // resident CTAs per SM the register budget is sized for: three where the
+  // accumulators and weight runs fit in 85 registers without spilling
+  static constexpr int kMinCtas = (MT == 1 && R16 <= 2) ? 3 : 2;
   static constexpr int kLutBytes = FMT == kFmtNF4 ? kNf4LutBytes : 0;
   // per warp, row group and token tile: a 16 x 8 f32 fragment
   static constexpr int kRedBytes = kWarps * R16 * MT * 128 * 4;
@@ -110,7 +113,7 @@ __device__ __forceinline__ void decode_half(const RowRun<FMT>& r, int h, uint32_
 }
 
 template <int FMT, int MT, int R16>
-__global__ void __launch_bounds__(SmallMCfg<FMT, MT, R16>::kThreads, 2)
+__global__ void __launch_bounds__(SmallMCfg<FMT, MT, R16>::kThreads, SmallMCfg<FMT, MT, R16>::kMinCtas)
     smallm_kernel(const __nv_bfloat16* __restrict__ x, const uint8_t* __restrict__ w,
                   const float* __restrict__ absmax, float fp8_scale,
                   const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ y, int M,
