@@ -702,6 +702,7 @@ def run_flux(args, world, rank, local):
             m.forward = fwd
         return saved
 
+    flux.FUSED_QKV = False  # the reference calls q, k and v as three linears
     saved = swap_forward(lambda m: rdq.nf4(m.weight_nf4, m.weight_absmax, m.out_features,
                                            m.in_features))
     ref_ms = timed(max(3, args.steps // 2))
@@ -713,6 +714,7 @@ def run_flux(args, world, rank, local):
     engine_dq_ms = timed(max(3, args.steps // 2))
     for m, f in saved:
         m.forward = f
+    flux.FUSED_QKV = True
     del rdq
     if rank == 0:
         cast_flops = 59.50e12  # cast linears per step at 1024x1024, B = 1

@@ -71,6 +71,9 @@ def heads_to_tokens(x, s_txt: int):
 # AdaLN modulation and gated residuals as one kernel each (False: the
 # reference's chain of tensor ops).
 FUSED_ADALN = True
+# q/k/v projections through one concatenated NF4 linear where fuse_qkv_projections
+# built it (False: three linears, as the reference calls them).
+FUSED_QKV = True
 
 
 def _rows(t):
@@ -352,6 +355,16 @@ class FluxAttention(nn.Module):
             return out
         return self.to_out[0](out)
 
+    @staticmethod
+    def _qkv(x, fused, q_proj, k_proj, v_proj):
+        """q, k, v projections of x: one concatenated NF4 linear (column views
+        of its output, read in place by the attention glue) or three."""
+        if FUSED_QKV and fused is not None:
+            y = fused(x)
+            n = q_proj.out_features
+            return y[..., :n], y[..., n:2 * n], y[..., 2 * n:]
+        return q_proj(x), k_proj(x), v_proj(x)
+
     def _forward_fused(self, x, ctx, rope):
         """The same computation with the norm / concat / transpose / rotary
         chain in one kernel per tensor and the split back in one more."""
@@ -359,11 +372,13 @@ class FluxAttention(nn.Module):
         q_t = k_t = v_t = None
         wq_t = wk_t = None
         if ctx is not None:
-            q_t, k_t, v_t = self.add_q_proj(ctx), self.add_k_proj(ctx), self.add_v_proj(ctx)
+            q_t, k_t, v_t = self._qkv(ctx, getattr(self, "add_qkv", None), self.add_q_proj,
+                                      self.add_k_proj, self.add_v_proj)
             wq_t, wk_t = self.norm_added_q.weight, self.norm_added_k.weight
-        q = qk_norm_rope(self.to_q(x), q_t, h, self.norm_q.weight, wq_t, rope, self.norm_q.eps)
-        k = qk_norm_rope(self.to_k(x), k_t, h, self.norm_k.weight, wk_t, rope, self.norm_k.eps)
-        v = qk_norm_rope(self.to_v(x), v_t, h)
+        q_i, k_i, v_i = self._qkv(x, getattr(self, "to_qkv", None), self.to_q, self.to_k, self.to_v)
+        q = qk_norm_rope(q_i, q_t, h, self.norm_q.weight, wq_t, rope, self.norm_q.eps)
+        k = qk_norm_rope(k_i, k_t, h, self.norm_k.weight, wk_t, rope, self.norm_k.eps)
+        v = qk_norm_rope(v_i, v_t, h)
         out = F.scaled_dot_product_attention(q, k, v, dropout_p=0.0, is_causal=False)
         txt_len = 0 if ctx is None else ctx.shape[1]
         txt, img = heads_to_tokens(out, txt_len)
@@ -509,12 +524,56 @@ def init_random_(model: nn.Module, seed: int = 0, std: float = 0.02):
     return model
 
 
-def build_flux_nf4(device="cuda", seed: int = 0, **config) -> FluxTransformer:
+def concat_nf4_linears(mods):
+    """One NF4 linear whose output features are those of `mods`, in order.
+    NF4 blocks of 64 never straddle a weight row, so a row range's packed codes
+    and block scales are contiguous: concatenating the buffers concatenates
+    the rows, with no repacking.  None unless every module is NF4 with the same
+    in_features."""
+    if not mods or any(not isinstance(m, modules.Ltx23Nf4Linear) for m in mods):
+        return None
+    k = mods[0].in_features
+    if any(m.in_features != k for m in mods):
+        return None
+    dev = mods[0].weight_nf4.device
+    fused = modules.Ltx23Nf4Linear(sum(m.out_features for m in mods), k, bias=False).to(dev)
+    fused.set_nf4_weight(torch.cat([m.weight_nf4 for m in mods]),
+                         torch.cat([m.weight_absmax for m in mods]))
+    if any(m.bias is not None for m in mods):
+        dt = next(m.bias.dtype for m in mods if m.bias is not None)
+        fused.bias = nn.Parameter(torch.cat([
+            m.bias.detach().to(dt) if m.bias is not None
+            else torch.zeros(m.out_features, dtype=dt, device=dev) for m in mods]), requires_grad=False)
+    return fused
+
+
+def fuse_qkv_projections(model):
+    """Give every attention of `model` a concatenated q/k/v NF4 linear per
+    stream (``to_qkv``, and ``add_qkv`` for the text stream): one wider GEMM
+    instead of three, its output read in place by the attention glue.  The
+    separate projections stay (the tensor-op path and the reference-algorithm
+    timing use them)."""
+    attns = [m for m in model.modules() if isinstance(m, FluxAttention)]
+    for a in attns:
+        f = concat_nf4_linears([a.to_q, a.to_k, a.to_v])
+        if f is not None:
+            a.to_qkv = f
+        if a.added_kv:
+            f = concat_nf4_linears([a.add_q_proj, a.add_k_proj, a.add_v_proj])
+            if f is not None:
+                a.add_qkv = f
+    return model
+
+
+def build_flux_nf4(device="cuda", seed: int = 0, fuse_qkv: bool = True, **config) -> FluxTransformer:
     """FLUX.1 transformer in bf16 with random weights and its 494 cast-set
-    linears replaced by fused NF4 linears (R/quantize_flux.R:541-576)."""
+    linears replaced by fused NF4 linears (R/quantize_flux.R:541-576); with
+    fuse_qkv each attention also gets its concatenated q/k/v linears."""
     with torch.device(device):
         model = FluxTransformer(**config).to(torch.bfloat16)
     init_random_(model, seed)
     modules.swap_quant_linears(model, modules.flux_is_quant_key, "nf4")
+    if fuse_qkv:
+        fuse_qkv_projections(model)
     torch.cuda.empty_cache()
     return model.eval()

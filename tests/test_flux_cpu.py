@@ -82,3 +82,30 @@ def test_cast_set_has_494_weights_at_full_size():
         model = flux.FluxTransformer()
     keys = [n for n, _ in model.named_parameters() if modules.flux_is_quant_key(n)]
     assert len(keys) == 494
+
+
+def test_concat_nf4_linears_concatenates_rows():
+    # NF4 rows are contiguous byte ranges: the concatenated module's buffers
+    # decode to the stacked weights of the parts, biases follow (a missing
+    # bias reads as zeros), and mixed input widths are refused
+    from diffuser_b200 import flux, modules
+    from oracle import torch_ref as T
+    torch.manual_seed(0)
+    parts = []
+    for n, with_bias in ((64, True), (128, False), (192, True)):
+        m = modules.Ltx23Nf4Linear(n, 256, bias=with_bias)
+        p, a = T.ltx23_nf4_quantize(torch.randn(n, 256) * 0.02)
+        m.set_nf4_weight(p, a)
+        if with_bias:
+            with torch.no_grad():
+                m.bias.copy_(torch.randn(n))
+        parts.append(m.to(torch.bfloat16))
+    fused = flux.concat_nf4_linears(parts)
+    assert fused.out_features == 384 and fused.in_features == 256
+    w = T.ltx23_nf4_dequantize(fused.weight_nf4, fused.weight_absmax, (384, 256))
+    ref = torch.cat([T.ltx23_nf4_dequantize(m.weight_nf4, m.weight_absmax, (m.out_features, 256))
+                     for m in parts])
+    assert torch.equal(w.view(torch.int16), ref.view(torch.int16))
+    assert torch.equal(fused.bias[:64], parts[0].bias) and not fused.bias[64:192].any()
+    assert torch.equal(fused.bias[192:], parts[2].bias)
+    assert flux.concat_nf4_linears([parts[0], modules.Ltx23Nf4Linear(8, 128)]) is None

@@ -59,15 +59,37 @@ def test_flux_dit_fused_matches_reference_backend():
     with torch.no_grad():
         out = flux.sample(model, x, text, pooled, rope, sigmas)
         ref_backend = _ReferenceBackend(model)
+        flux.FUSED_QKV = False  # the reference calls q, k and v separately
         try:
             ref = flux.sample(model, x, text, pooled, rope, sigmas)
         finally:
             ref_backend.restore()
+            flux.FUSED_QKV = True
     torch.cuda.synchronize()
     assert ops.device_error() == 0
     assert torch.isfinite(out.float()).all()
     cos = torch.nn.functional.cosine_similarity(out.float().flatten(), ref.float().flatten(), dim=0)
     assert cos.item() >= 0.999, cos.item()
+
+
+def test_concatenated_qkv_projection_matches_separate_linears():
+    # one NF4 linear over the concatenated q/k/v rows gives the three
+    # projections' outputs (text stream: 512 tokens, image: 4096)
+    from diffuser_b200 import flux
+    from oracle import numpy_ref as R
+    from tests.gpu_util import to_bits
+    dev = torch.device("cuda", 0)
+    model = flux.build_flux_nf4(dev, seed=3, num_layers=1, num_single_layers=1)
+    attn = model.transformer_blocks[0].attn
+    for fused, parts, m in ((attn.to_qkv, (attn.to_q, attn.to_k, attn.to_v), 4096),
+                            (attn.add_qkv, (attn.add_q_proj, attn.add_k_proj, attn.add_v_proj), 512)):
+        x = torch.randn(1, m, 3072, device=dev).to(torch.bfloat16)
+        with torch.no_grad():
+            y = fused(x)
+            ref = torch.cat([p(x) for p in parts], dim=-1)
+        assert y.shape == ref.shape
+        assert R.rel_err(to_bits(y.reshape(m, -1)), to_bits(ref.reshape(m, -1))) <= 1e-2
+        assert (y != ref).float().mean().item() < 0.01
 
 
 def test_flux_step_captures_in_a_cuda_graph():
