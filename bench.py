@@ -57,6 +57,8 @@ def parse():
                     default="nf4")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--profile-kernels", action="store_true",
+                    help="flux_dit: add the per-kernel device-time table of one eager step")
     return ap.parse_args()
 
 
@@ -685,6 +687,19 @@ def run_flux(args, world, rank, local):
         ms = timed_graph(args.steps)
     err = ops.device_error(dev)
     del graph, step_out
+    kernels = None
+    if args.profile_kernels:
+        # one eager step under the torch profiler (outside every timed region)
+        torch.cuda.synchronize()
+        with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+            step()
+            torch.cuda.synchronize()
+        ka = prof.key_averages()
+        total = sum(e.device_time_total for e in ka)
+        kernels = {"total_ms": total / 1e3,
+                   "top": [{"kernel": e.key[:120], "launches": e.count, "ms": e.device_time_total / 1e3,
+                            "share": e.device_time_total / total}
+                           for e in sorted(ka, key=lambda e: -e.device_time_total)[:16]]}
     # The reference's algorithm for every NF4 linear, same weights: its
     # libtorch decode ops into a per-shape bf16 buffer, then cuBLAS; and, for
     # context, the engine's standalone dequantize kernel in place of those ops.
@@ -702,7 +717,8 @@ def run_flux(args, world, rank, local):
             m.forward = fwd
         return saved
 
-    flux.FUSED_QKV = False  # the reference calls q, k and v as three linears
+    # the reference calls q, k and v as three linears and concatenates with torch.cat
+    flux.FUSED_QKV = flux.FUSED_CONCAT = False
     saved = swap_forward(lambda m: rdq.nf4(m.weight_nf4, m.weight_absmax, m.out_features,
                                            m.in_features))
     ref_ms = timed(max(3, args.steps // 2))
@@ -714,7 +730,7 @@ def run_flux(args, world, rank, local):
     engine_dq_ms = timed(max(3, args.steps // 2))
     for m, f in saved:
         m.forward = f
-    flux.FUSED_QKV = True
+    flux.FUSED_QKV = flux.FUSED_CONCAT = True
     del rdq
     if rank == 0:
         cast_flops = 59.50e12  # cast linears per step at 1024x1024, B = 1
@@ -737,6 +753,8 @@ def run_flux(args, world, rank, local):
                     "engine-dequantize + cuBLAS step are eager",
             "device_error": err, "clocks": clk.summary(),
         }
+        if kernels is not None:
+            line["kernels_one_eager_step"] = kernels
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

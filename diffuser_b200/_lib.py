@@ -53,6 +53,15 @@ SIGNATURES = {
     "dq_heads_to_tokens": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                           ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
                                           ctypes.c_void_p]),
+    "dq_linear_nf4_ld": (ctypes.c_int, [ctypes.c_void_p, _c_i64, _c_i64, ctypes.c_void_p, ctypes.c_void_p,
+                                        ctypes.c_void_p, _c_i64, ctypes.c_int, ctypes.c_void_p, _c_i64,
+                                        ctypes.c_void_p, _c_sz, ctypes.c_void_p]),
+    "dq_linear_fp8_ld": (ctypes.c_int, [ctypes.c_void_p, _c_i64, _c_i64, ctypes.c_void_p, ctypes.c_float,
+                                        ctypes.c_void_p, _c_i64, ctypes.c_int, ctypes.c_void_p, _c_i64,
+                                        ctypes.c_void_p, _c_sz, ctypes.c_void_p]),
+    "dq_heads_to_tokens_ld": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                             ctypes.c_int, ctypes.c_int, ctypes.c_void_p, _c_i64,
+                                             ctypes.c_void_p, _c_i64, ctypes.c_void_p]),
     "dq_adaln_modulate": (ctypes.c_int, [ctypes.c_void_p, _c_i64, _c_i64, ctypes.c_int, ctypes.c_int,
                                          ctypes.c_void_p, ctypes.c_void_p, _c_i64, ctypes.c_float,
                                          ctypes.c_void_p, _c_i64, ctypes.c_void_p]),

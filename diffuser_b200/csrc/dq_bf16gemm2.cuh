@@ -360,7 +360,7 @@ __global__ void __launch_bounds__(Bf16PairCfg<BM, FMT>::kThreads, 1)
           const int m = mrow0 + row;
           const int nc = ncol0 + col;
           if (m < args.M) {
-            __nv_bfloat16* dst = y + static_cast<size_t>(m) * args.N + nc;
+            __nv_bfloat16* dst = y + static_cast<size_t>(m) * args.ldy + nc;
             if (args.vec_ok && nc + 8 <= args.N) {
               *reinterpret_cast<uint4*>(dst) = lds128(stg_s + 2u * (row * 32 + col));
             } else {

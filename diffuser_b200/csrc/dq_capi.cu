@@ -151,17 +151,18 @@ __global__ void tp_wait_kernel(const unsigned int* flags, int world, unsigned in
   }
 }
 
-// Split-K: y = bf16(sum_s partial[s] + bias); four outputs per thread.
+// Split-K: y[m, n] (row stride ldy) = bf16(sum_s partial[s][m, n] + bias).
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int M, int N,
                                      const __nv_bfloat16* __restrict__ bias,
-                                     __nv_bfloat16* __restrict__ y, int act) {
+                                     __nv_bfloat16* __restrict__ y, int act, int64_t ldy) {
   const int64_t total = static_cast<int64_t>(M) * N;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total; i += stride) {
     float acc = 0.f;
     for (int s = 0; s < splits; ++s) acc += part[static_cast<size_t>(s) * total + i];
-    if (bias != nullptr) acc += __bfloat162float(bias[i % N]);
-    y[i] = __float2bfloat16_rn(apply_act(acc, act));
+    const int64_t m = i / N, n = i - m * N;
+    if (bias != nullptr) acc += __bfloat162float(bias[n]);
+    y[m * ldy + n] = __float2bfloat16_rn(apply_act(acc, act));
   }
 }
 
@@ -608,7 +609,7 @@ static constexpr unsigned long long kTpWaitNs = 5000000000ull;  // 5 s
 template <int FMT, int MT, int R16>
 static int launch_smallm_cfg(DeviceInfo* d, const Plan& p, const void* x, const uint8_t* w,
                              const float* absmax, float scale, const void* bias, void* y,
-                             int64_t M, int64_t N, int64_t K, int act, cudaStream_t st) {
+                             int64_t M, int64_t N, int64_t K, int act, int64_t ldy, cudaStream_t st) {
   using C = SmallMCfg<FMT, MT, R16>;
   auto kern = smallm_kernel<FMT, MT, R16>;
   int& set = d->smallm_set[FMT][MT - 1][R16 == 4 ? 2 : R16 - 1];
@@ -621,30 +622,33 @@ static int launch_smallm_cfg(DeviceInfo* d, const Plan& p, const void* x, const 
   kern<<<p.grid, C::kThreads, C::kSmemBytes, st>>>(
       static_cast<const __nv_bfloat16*>(x), w, absmax, scale,
       static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y),
-      static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), act);
+      static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), act, ldy);
   return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
 }
 
 template <int FMT, int MT>
 static int launch_smallm(DeviceInfo* d, const Plan& p, const void* x, const uint8_t* w,
                          const float* absmax, float scale, const void* bias, void* y, int64_t M,
-                         int64_t N, int64_t K, int act, cudaStream_t st) {
+                         int64_t N, int64_t K, int act, int64_t ldy, cudaStream_t st) {
   switch (smallm_r16(FMT, M, N, d->sms)) {
     case 4:
       if constexpr (MT == 1)
-        return launch_smallm_cfg<FMT, MT, 4>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, st);
+        return launch_smallm_cfg<FMT, MT, 4>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
       break;
     case 2:
-      return launch_smallm_cfg<FMT, MT, 2>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, st);
+      return launch_smallm_cfg<FMT, MT, 2>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
   }
-  return launch_smallm_cfg<FMT, MT, 1>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, st);
+  return launch_smallm_cfg<FMT, MT, 1>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
 }
 
 static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8_t* w,
                        const float* absmax, float scale, const void* bias, int64_t N, void* y,
                        void* ws, size_t ws_bytes, cudaStream_t st, const TpOpts* tp = nullptr,
-                       bool allow_twophase = true, int act = kActNone) {
+                       bool allow_twophase = true, int act = kActNone, int64_t ldy = 0) {
   if (act != kActNone && act != kActGeluTanh) return DQ_ERR_ARG;
+  // y row stride (elements): N unless the caller writes into a wider buffer
+  if (ldy == 0) ldy = N;
+  if (ldy < N || ldy > INT32_MAX || (tp != nullptr && ldy != N)) return DQ_ERR_SHAPE;
   // NF4 blocks of 64 must lie inside a weight row; fp8 needs only 16-byte
   // row strides for TMA (the ragged last k-block is zero-filled).
   if (M < 0 || N <= 0 || K <= 0 || (K % (fmt == kFmtNF4 ? 64 : 16)) != 0) return DQ_ERR_SHAPE;
@@ -664,10 +668,10 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
 
   if (p.smallm) {
     if (fmt == kFmtNF4)
-      return p.bm <= 8 ? launch_smallm<kFmtNF4, 1>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, st)
-                       : launch_smallm<kFmtNF4, 2>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, st);
-    return p.bm <= 8 ? launch_smallm<kFmtFP8, 1>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, st)
-                     : launch_smallm<kFmtFP8, 2>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, st);
+      return p.bm <= 8 ? launch_smallm<kFmtNF4, 1>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st)
+                       : launch_smallm<kFmtNF4, 2>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
+    return p.bm <= 8 ? launch_smallm<kFmtFP8, 1>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st)
+                     : launch_smallm<kFmtFP8, 2>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
   }
 
   if (p.twophase) {
@@ -723,9 +727,9 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
     }
     g.outs[0] = y;
     g.n_out = 1;
-    g.ldy = static_cast<int>(N);
+    g.ldy = static_cast<int>(ldy);
     g.col0 = 0;
-    g.vec_ok = (N % 8 == 0) && aligned(y, 16);
+    g.vec_ok = (N % 8 == 0) && (ldy % 8 == 0) && aligned(y, 16);
     g.tp_counter = nullptr;
     g.tp_rank = 0;
     g.tp_epoch = 0;
@@ -779,9 +783,9 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
   } else if (tp == nullptr) {
     a.outs[0] = y;
     a.n_out = 1;
-    a.ldy = static_cast<int>(N);
+    a.ldy = static_cast<int>(ldy);
     a.col0 = 0;
-    a.vec_ok = (N % 8 == 0) && aligned(y, 16);
+    a.vec_ok = (N % 8 == 0) && (ldy % 8 == 0) && aligned(y, 16);
   } else {
     a.n_out = tp->world;
     a.ldy = static_cast<int>(N * tp->world);
@@ -808,7 +812,7 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
     const int64_t total = M * N;
     splitk_reduce_kernel<<<grid_for(total, 256, d->sms), 256, 0, st>>>(
         static_cast<const float*>(ws), p.splits, a.M, a.N, a.bias,
-        static_cast<__nv_bfloat16*>(y), a.act);
+        static_cast<__nv_bfloat16*>(y), a.act, ldy);
     if (cudaGetLastError() != cudaSuccess) return DQ_ERR_LAUNCH;
   }
   if (tp != nullptr) {
@@ -953,6 +957,22 @@ size_t dq_workspace_size(int64_t M, int64_t N, int64_t K, int fmt) {
   DeviceInfo* d = nullptr;
   if (current_device(&d) != DQ_OK || d == nullptr) return 0;
   return make_plan(fmt, M, N, K, d->sms).ws;
+}
+
+int dq_linear_nf4_ld(const void* x, int64_t M, int64_t K, const uint8_t* packed,
+                     const float* absmax, const void* bias, int64_t N, int act, void* y,
+                     int64_t ldy, void* workspace, size_t workspace_bytes, dq_stream_t stream) {
+  if (ldy < N) return DQ_ERR_SHAPE;
+  return linear_impl(kFmtNF4, x, M, K, packed, absmax, 0.f, bias, N, y, workspace, workspace_bytes,
+                     static_cast<cudaStream_t>(stream), nullptr, true, act, ldy);
+}
+
+int dq_linear_fp8_ld(const void* x, int64_t M, int64_t K, const uint8_t* w8, float scale,
+                     const void* bias, int64_t N, int act, void* y, int64_t ldy, void* workspace,
+                     size_t workspace_bytes, dq_stream_t stream) {
+  if (ldy < N) return DQ_ERR_SHAPE;
+  return linear_impl(kFmtFP8, x, M, K, w8, nullptr, scale, bias, N, y, workspace, workspace_bytes,
+                     static_cast<cudaStream_t>(stream), nullptr, true, act, ldy);
 }
 
 int dq_linear_nf4_ex(const void* x, int64_t M, int64_t K, const uint8_t* packed,
@@ -1149,6 +1169,12 @@ int dq_qk_norm_rope(const void* img, int64_t ld_img, const void* txt, int64_t ld
 
 int dq_heads_to_tokens(const void* in, int B, int H, int S_txt, int S_img, int D, void* out_txt,
                        void* out_img, dq_stream_t stream) {
+  const int64_t hd = static_cast<int64_t>(H) * D;
+  return dq_heads_to_tokens_ld(in, B, H, S_txt, S_img, D, out_txt, hd, out_img, hd, stream);
+}
+
+int dq_heads_to_tokens_ld(const void* in, int B, int H, int S_txt, int S_img, int D, void* out_txt,
+                          int64_t ld_txt, void* out_img, int64_t ld_img, dq_stream_t stream) {
   if (B <= 0 || H <= 0 || S_txt < 0 || S_img < 0 || D <= 0 || D % 64 != 0 || D > 256)
     return DQ_ERR_SHAPE;
   if (in == nullptr || out_img == nullptr || (S_txt > 0 && out_txt == nullptr)) return DQ_ERR_ARG;
@@ -1160,9 +1186,13 @@ int dq_heads_to_tokens(const void* in, int B, int H, int S_txt, int S_img, int D
   const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(in);
   __nv_bfloat16* ot = static_cast<__nv_bfloat16*>(out_txt);
   __nv_bfloat16* oi = static_cast<__nv_bfloat16*>(out_img);
-  const bool vec = aligned(in, 16) && aligned(out_txt, 16) && aligned(out_img, 16);
+  if (ld_img < static_cast<int64_t>(H) * D || (S_txt > 0 && ld_txt < static_cast<int64_t>(H) * D))
+    return DQ_ERR_SHAPE;
+  const bool vec = aligned(in, 16) && aligned(out_txt, 16) && aligned(out_img, 16) &&
+                   ld_img % 8 == 0 && (S_txt == 0 || ld_txt % 8 == 0);
   auto launch = [&](auto kern) {
-    kern<<<static_cast<int>(blocks), threads, 0, st>>>(src, B, H, S_txt, S_img, ot, oi);
+    kern<<<static_cast<int>(blocks), threads, 0, st>>>(src, B, H, S_txt, S_img, ot, ld_txt, oi,
+                                                       ld_img);
   };
   switch (D / 32) {
     case 2: vec ? launch(heads_to_tokens_kernel<2, true>) : launch(heads_to_tokens_kernel<2, false>); break;

@@ -175,7 +175,8 @@ __global__ void __launch_bounds__(512)
 template <int EPL, bool VEC>
 __global__ void __launch_bounds__(512)
     heads_to_tokens_kernel(const __nv_bfloat16* __restrict__ in, int B, int H, int S_txt, int S_img,
-                           __nv_bfloat16* __restrict__ out_txt, __nv_bfloat16* __restrict__ out_img) {
+                           __nv_bfloat16* __restrict__ out_txt, int64_t ld_txt,
+                           __nv_bfloat16* __restrict__ out_img, int64_t ld_img) {
   constexpr int D = EPL * 32;
   constexpr int HPW = kHeadsPerWarp;
   const int lane = threadIdx.x & 31;
@@ -184,9 +185,8 @@ __global__ void __launch_bounds__(512)
   const int S = S_txt + S_img;
   const int b = static_cast<int>(blockIdx.x) / S;
   const int s = static_cast<int>(blockIdx.x) - b * S;
-  __nv_bfloat16* drow =
-      s < S_txt ? out_txt + (static_cast<int64_t>(b) * S_txt + s) * H * D
-                : out_img + (static_cast<int64_t>(b) * S_img + (s - S_txt)) * H * D;
+  __nv_bfloat16* drow = s < S_txt ? out_txt + (static_cast<int64_t>(b) * S_txt + s) * ld_txt
+                                  : out_img + (static_cast<int64_t>(b) * S_img + (s - S_txt)) * ld_img;
   for (int h0 = warp * HPW; h0 < H; h0 += nwarps * HPW) {
     float v[HPW][EPL];
 #pragma unroll

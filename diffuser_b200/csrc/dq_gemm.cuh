@@ -87,7 +87,8 @@ struct GemmArgs {
   int vec_ok;                 // 16-byte vector stores are aligned for every destination
   // bf16 Y destinations (splits == 1): element (m, n) goes to
   // outs[d][m * ldy + col0 + n] for every d < n_out.  One destination with
-  // ldy = N, col0 = 0 normally; every rank's y [M, N_total] (possibly peer
+  // col0 = 0 and the caller's row stride ldy (N unless y is a column range of
+  // a wider buffer) normally; every rank's y [M, N_total] (possibly peer
   // memory) in the column-parallel linear.
   void* outs[kMaxRanks];
   int n_out, ldy, col0;
@@ -635,8 +636,7 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
             const int m = mrow0 + row;
             const int nc = ncol0 + col;
             if (m < args.M) {
-              const size_t off = TP ? static_cast<size_t>(m) * args.ldy + args.col0 + nc
-                                    : static_cast<size_t>(m) * args.N + nc;
+              const size_t off = static_cast<size_t>(m) * args.ldy + args.col0 + nc;
               if (args.vec_ok && nc + 8 <= args.N) {
                 const uint4 v16 = lds128(stg_s + 2u * (row * 32 + col));
                 if constexpr (TP) {

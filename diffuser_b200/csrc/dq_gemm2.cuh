@@ -431,8 +431,7 @@ __global__ void __launch_bounds__(Gemm2Cfg<FMT, BM>::kThreads, 1)
             const int m = mrow0 + row;
             const int nc = ncol0 + col;
             if (m < args.M) {
-              const size_t off = TP ? static_cast<size_t>(m) * args.ldy + args.col0 + nc
-                                    : static_cast<size_t>(m) * args.N + nc;
+              const size_t off = static_cast<size_t>(m) * args.ldy + args.col0 + nc;
               if (args.vec_ok && nc + 8 <= args.N) {
                 const uint4 v16 = lds128(stg_s + 2u * (row * 32 + col));
                 if constexpr (TP) {

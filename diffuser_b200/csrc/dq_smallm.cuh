@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(SmallMCfg<FMT, MT, R16>::kThreads, SmallMCfg<F
     smallm_kernel(const __nv_bfloat16* __restrict__ x, const uint8_t* __restrict__ w,
                   const float* __restrict__ absmax, float fp8_scale,
                   const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ y, int M,
-                  int N, int K, int act) {
+                  int N, int K, int act, int64_t ldy) {
   using C = SmallMCfg<FMT, MT, R16>;
   constexpr bool PF = C::kPrefetch;
   extern __shared__ __align__(16) uint8_t smem[];
@@ -226,7 +226,7 @@ __global__ void __launch_bounds__(SmallMCfg<FMT, MT, R16>::kThreads, SmallMCfg<F
     const int m = 8 * mt + tok;
     if (n < N && m < M) {
       if (bias != nullptr) s += __bfloat162float(bias[n]);
-      y[static_cast<int64_t>(m) * N + n] = __float2bfloat16_rn(apply_act(s, act));
+      y[static_cast<int64_t>(m) * ldy + n] = __float2bfloat16_rn(apply_act(s, act));
     }
   }
 }

@@ -55,16 +55,25 @@ def qk_norm_rope(img, txt, heads: int, w_img=None, w_txt=None, rope=None, eps: f
     return out
 
 
-def heads_to_tokens(x, s_txt: int):
-    """[B, H, S_txt + S_img, D] -> (txt [B, S_txt, H*D] or None, img [B, S_img, H*D])."""
+def heads_to_tokens(x, s_txt: int, img_out=None):
+    """[B, H, S_txt + S_img, D] -> (txt [B, S_txt, H*D] or None, img [B, S_img, H*D]);
+    img_out, if given, is a [B, S_img, H*D] view (e.g. the first columns of a
+    wider buffer) that receives the image tokens."""
     b, h, s, d = x.shape
     x = x if x.is_contiguous() else x.contiguous()
     s_img = s - s_txt
-    img = torch.empty((b, s_img, h * d), dtype=torch.bfloat16, device=x.device)
+    if img_out is None:
+        img = torch.empty((b, s_img, h * d), dtype=torch.bfloat16, device=x.device)
+        ld_img = h * d
+    else:
+        img, ld_img = _rows(img_out)
+        if img.data_ptr() != img_out.data_ptr():
+            raise ValueError("img_out must have evenly spaced rows with unit feature stride")
     txt = torch.empty((b, s_txt, h * d), dtype=torch.bfloat16, device=x.device) if s_txt else None
     stream = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
-    rc = _lib.lib().dq_heads_to_tokens(_ptr(x), b, h, s_txt, s_img, d, _ptr(txt), _ptr(img), stream)
-    _lib.check("dq_heads_to_tokens", rc)
+    rc = _lib.lib().dq_heads_to_tokens_ld(_ptr(x), b, h, s_txt, s_img, d, _ptr(txt), h * d,
+                                          _ptr(img), ld_img, stream)
+    _lib.check("dq_heads_to_tokens_ld", rc)
     return txt, img
 
 
@@ -74,6 +83,9 @@ FUSED_ADALN = True
 # q/k/v projections through one concatenated NF4 linear where fuse_qkv_projections
 # built it (False: three linears, as the reference calls them).
 FUSED_QKV = True
+# Single blocks: attention and MLP outputs written into the two column ranges
+# of proj_out's input (False: torch.cat of the two, as the reference does).
+FUSED_CONCAT = True
 
 
 def _rows(t):
@@ -139,12 +151,19 @@ def _gated_add(x, gate, y):
 FUSED_GELU = True
 
 
-def _proj_gelu_tanh(proj, x):
+def _proj_gelu_tanh(proj, x, out=None):
     """GELU-tanh of a projection; fused into the quantized linear's epilogue on
-    the engine (the projection is still rounded to bf16 before the activation)."""
+    the engine (the projection is still rounded to bf16 before the activation).
+    With `out` the result is written there."""
     if FUSED_GELU and isinstance(proj, (modules.Ltx23Nf4Linear, modules.Ltx23Fp8Linear)) and x.is_cuda:
-        return proj(x, act="gelu_tanh")
-    return F.gelu(proj(x), approximate="tanh")
+        if out is None:  # forwards that predate `out` keep working
+            return proj(x, act="gelu_tanh")
+        return proj(x, act="gelu_tanh", out=out)
+    y = F.gelu(proj(x), approximate="tanh")
+    if out is None:
+        return y
+    out.copy_(y)
+    return out
 
 
 # --------------------------------------------------------------- primitives
@@ -325,10 +344,10 @@ class FluxAttention(nn.Module):
             self.add_v_proj = nn.Linear(dim, inner)
             self.to_add_out = nn.Linear(inner, dim)
 
-    def forward(self, x, ctx=None, rope=None):
+    def forward(self, x, ctx=None, rope=None, out=None):
         h = self.heads
         if _fused_ok(x, self.norm_q.weight.shape[0]):
-            return self._forward_fused(x, ctx, rope)
+            return self._forward_fused(x, ctx, rope, out)
         q = self.norm_q(self.to_q(x).unflatten(-1, (h, -1)))
         k = self.norm_k(self.to_k(x).unflatten(-1, (h, -1)))
         v = self.to_v(x).unflatten(-1, (h, -1))
@@ -365,7 +384,7 @@ class FluxAttention(nn.Module):
             return y[..., :n], y[..., n:2 * n], y[..., 2 * n:]
         return q_proj(x), k_proj(x), v_proj(x)
 
-    def _forward_fused(self, x, ctx, rope):
+    def _forward_fused(self, x, ctx, rope, out=None):
         """The same computation with the norm / concat / transpose / rotary
         chain in one kernel per tensor and the split back in one more."""
         h = self.heads
@@ -379,9 +398,10 @@ class FluxAttention(nn.Module):
         q = qk_norm_rope(q_i, q_t, h, self.norm_q.weight, wq_t, rope, self.norm_q.eps)
         k = qk_norm_rope(k_i, k_t, h, self.norm_k.weight, wk_t, rope, self.norm_k.eps)
         v = qk_norm_rope(v_i, v_t, h)
-        out = F.scaled_dot_product_attention(q, k, v, dropout_p=0.0, is_causal=False)
+        att = F.scaled_dot_product_attention(q, k, v, dropout_p=0.0, is_causal=False)
         txt_len = 0 if ctx is None else ctx.shape[1]
-        txt, img = heads_to_tokens(out, txt_len)
+        # `out` (pre-only attention): the image tokens go straight there
+        txt, img = heads_to_tokens(att, txt_len, out if (self.pre_only and ctx is None) else None)
         if ctx is not None:
             return self.to_out[0](img), self.to_add_out(txt)
         if self.pre_only:
@@ -429,6 +449,16 @@ class SingleBlock(nn.Module):
 
     def forward(self, x, temb, rope):
         n, gate = self.norm(x, temb)
+        if FUSED_CONCAT and _fused_ok(n, self.attn.norm_q.weight.shape[0]) and \
+                isinstance(self.proj_mlp, (modules.Ltx23Nf4Linear, modules.Ltx23Fp8Linear)):
+            # attention and MLP outputs land in the two column ranges of the
+            # proj_out input, which is then read whole (no concatenation pass)
+            d_attn = self.attn.to_q.out_features
+            cat = torch.empty(*n.shape[:-1], d_attn + self.proj_mlp.out_features,
+                              dtype=torch.bfloat16, device=n.device)
+            _proj_gelu_tanh(self.proj_mlp, n, out=cat[..., d_attn:])
+            self.attn(n, rope=rope, out=cat[..., :d_attn])
+            return _gated_add(x, gate, self.proj_out(cat))
         mlp = _proj_gelu_tanh(self.proj_mlp, n)
         a = self.attn(n, rope=rope)
         x = _gated_add(x, gate, self.proj_out(torch.cat([a, mlp], dim=2)))

@@ -52,9 +52,10 @@ class Ltx23Nf4Linear(nn.Module):
             self.weight_absmax = self.weight_absmax.to(torch.float32)
         return self
 
-    def forward(self, x: torch.Tensor, act: str | None = None) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, act: str | None = None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
         return ops.nf4_linear(x, self.weight_nf4, self.weight_absmax, self.out_features, self.bias,
-                              act=act)
+                              act=act, out=out)
 
     def extra_repr(self) -> str:
         return f"in_features={self.in_features}, out_features={self.out_features}, format=nf4"
@@ -95,14 +96,15 @@ class Ltx23Fp8Linear(nn.Module):
         self._resident = weight if weight.is_cuda else None
         return self
 
-    def forward(self, x: torch.Tensor, act: str | None = None) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, act: str | None = None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
         if self.weight_fp8 is None:
             raise RuntimeError("set_fp8_weight() has not been called")
         w8 = self._resident
         if w8 is None or w8.device != x.device:
             w8 = self.weight_fp8.to(device=x.device, non_blocking=True)
             self._resident = w8
-        return ops.fp8_linear(x, w8, self._scale_f, self.bias, act=act)
+        return ops.fp8_linear(x, w8, self._scale_f, self.bias, act=act, out=out)
 
     def extra_repr(self) -> str:
         return f"in_features={self.in_features}, out_features={self.out_features}, format=fp8"

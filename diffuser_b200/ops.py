@@ -175,17 +175,42 @@ def _prep_bias(bias, n: int, device):
 _ACTS = {None: _lib.DQ_ACT_NONE, "gelu_tanh": _lib.DQ_ACT_GELU_TANH}
 
 
+def _out_rows(out: torch.Tensor, m: int, n: int) -> int:
+    """Row stride (elements) of a caller-given output viewed as [m, n] rows,
+    which must be evenly spaced with unit stride along the features."""
+    if out.dtype != torch.bfloat16 or not out.is_cuda:
+        raise TypeError("out must be a bfloat16 CUDA tensor")
+    if out.shape[-1] != n or out.numel() != m * n or out.stride(-1) != 1:
+        raise ValueError(f"out must hold [{m}, {n}] with unit stride along the last dimension")
+    ld = out.stride(-2) if out.dim() >= 2 else n
+    for d in range(out.dim() - 2):
+        if out.stride(d) != out.shape[d + 1] * out.stride(d + 1):
+            raise ValueError("out's rows must be evenly spaced")
+    return ld
+
+
 def nf4_linear(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor,
-               out_features: int, bias: torch.Tensor | None = None, act: str | None = None) -> torch.Tensor:
+               out_features: int, bias: torch.Tensor | None = None, act: str | None = None,
+               out: torch.Tensor | None = None) -> torch.Tensor:
     """y = x . dequant_nf4(W)^T + bias (R/nf4_ltx23.R:235-246); act="gelu_tanh"
-    applies GELU-tanh in the epilogue, as gelu_proj does after the projection."""
+    applies GELU-tanh in the epilogue, as gelu_proj does after the projection.
+    With `out` (e.g. a column range of a wider buffer) y is written there."""
     n = int(out_features)
     k = packed.numel() * 2 // n
     x2 = _prep_x(x, k)
     m = x2.shape[0]
-    y = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
     b = _prep_bias(bias, n, x.device)
     am = absmax if absmax.dtype == torch.float32 else absmax.float()
+    if out is not None:
+        ldy = _out_rows(out, m, n)
+        with torch.cuda.device(x.device):
+            ws_bytes = workspace_size(m, n, k, _lib.DQ_FMT_NF4)
+            ws = workspace(x.device, ws_bytes)
+            _lib.check("dq_linear_nf4_ld", _lib.lib().dq_linear_nf4_ld(
+                _ptr(x2), m, k, _ptr(packed), _ptr(am), _ptr(b), n, _ACTS[act], _ptr(out), ldy,
+                _ptr(ws), ws_bytes, _stream(x.device)))
+        return out
+    y = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
     with torch.cuda.device(x.device):
         ws_bytes = workspace_size(m, n, k, _lib.DQ_FMT_NF4)
         ws = workspace(x.device, ws_bytes)
@@ -201,15 +226,26 @@ def nf4_linear(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor,
 
 
 def fp8_linear(x: torch.Tensor, w8: torch.Tensor, scale: float,
-               bias: torch.Tensor | None = None, act: str | None = None) -> torch.Tensor:
+               bias: torch.Tensor | None = None, act: str | None = None,
+               out: torch.Tensor | None = None) -> torch.Tensor:
     """y = x . (e4m3(W) * bf16(scale))^T + bias fused (R/fp8_ltx23.R:70-83);
-    act="gelu_tanh" applies GELU-tanh in the epilogue."""
+    act="gelu_tanh" applies GELU-tanh in the epilogue; with `out` y is written
+    there (its rows may be spaced wider than out_features)."""
     n, k = int(w8.shape[0]), int(w8.shape[1])
     x2 = _prep_x(x, k)
     m = x2.shape[0]
-    y = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
     b = _prep_bias(bias, n, x.device)
     raw = w8.view(torch.uint8)
+    if out is not None:
+        ldy = _out_rows(out, m, n)
+        with torch.cuda.device(x.device):
+            ws_bytes = workspace_size(m, n, k, _lib.DQ_FMT_FP8)
+            ws = workspace(x.device, ws_bytes)
+            _lib.check("dq_linear_fp8_ld", _lib.lib().dq_linear_fp8_ld(
+                _ptr(x2), m, k, _ptr(raw), ctypes.c_float(float(scale)), _ptr(b), n, _ACTS[act],
+                _ptr(out), ldy, _ptr(ws), ws_bytes, _stream(x.device)))
+        return out
+    y = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
     with torch.cuda.device(x.device):
         ws_bytes = workspace_size(m, n, k, _lib.DQ_FMT_FP8)
         ws = workspace(x.device, ws_bytes)

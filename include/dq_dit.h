@@ -33,6 +33,11 @@ int dq_qk_norm_rope(const void* img, int64_t ld_img, const void* txt, int64_t ld
 int dq_heads_to_tokens(const void* in, int B, int H, int S_txt, int S_img, int D, void* out_txt,
                        void* out_img, dq_stream_t stream);
 
+/* dq_heads_to_tokens with the outputs' row strides (elements, >= H*D): the
+ * tokens can land in a column range of a wider buffer. */
+int dq_heads_to_tokens_ld(const void* in, int B, int H, int S_txt, int S_img, int D, void* out_txt,
+                          int64_t ld_txt, void* out_img, int64_t ld_img, dq_stream_t stream);
+
 /* AdaLN-Zero modulation (R/dit_flux_modules.R:26-42 and 54-70; the norm2
  * lines of flux_double_block): x [T, D] (row stride ld_x, T = B * S tokens,
  * batch element t / S) -> out = bf16(bf16(bf16(LayerNorm(x)) * bf16(1 +

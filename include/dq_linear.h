@@ -192,6 +192,18 @@ int dq_linear_fp8_ex(const void* x, int64_t M, int64_t K, const uint8_t* w8, flo
                      const void* bias, int64_t N, int act, void* y, void* workspace,
                      size_t workspace_bytes, dq_stream_t stream);
 
+/* The NF4 / fp8 linear with an activation (as the *_ex entry points) writing
+ * y[m * ldy + n] (ldy >= N elements): the output can be a column range of a
+ * wider row-major buffer, e.g. one part of a concatenation that the next
+ * linear reads whole (no counterpart in the reference, which concatenates
+ * tensors with torch_cat).  Everything else as dq_linear_nf4 / dq_linear_fp8. */
+int dq_linear_nf4_ld(const void* x, int64_t M, int64_t K, const uint8_t* packed,
+                     const float* absmax, const void* bias, int64_t N, int act, void* y,
+                     int64_t ldy, void* workspace, size_t workspace_bytes, dq_stream_t stream);
+int dq_linear_fp8_ld(const void* x, int64_t M, int64_t K, const uint8_t* w8, float scale,
+                     const void* bias, int64_t N, int act, void* y, int64_t ldy, void* workspace,
+                     size_t workspace_bytes, dq_stream_t stream);
+
 /* Describes the launch plan dq_linear_* uses for this shape on the current
  * device: *pair = 0 for fused one-CTA tiles (128 weight rows), 1 for fused
  * CTA-pair tiles (256 rows), 2 for the two-phase plan (dequantize, then the

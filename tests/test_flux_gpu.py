@@ -59,12 +59,13 @@ def test_flux_dit_fused_matches_reference_backend():
     with torch.no_grad():
         out = flux.sample(model, x, text, pooled, rope, sigmas)
         ref_backend = _ReferenceBackend(model)
-        flux.FUSED_QKV = False  # the reference calls q, k and v separately
+        # the reference calls q, k and v separately and concatenates with torch.cat
+        flux.FUSED_QKV = flux.FUSED_CONCAT = False
         try:
             ref = flux.sample(model, x, text, pooled, rope, sigmas)
         finally:
             ref_backend.restore()
-            flux.FUSED_QKV = True
+            flux.FUSED_QKV = flux.FUSED_CONCAT = True
     torch.cuda.synchronize()
     assert ops.device_error() == 0
     assert torch.isfinite(out.float()).all()
@@ -147,6 +148,10 @@ def test_fused_attention_glue_wide_and_scalar_accesses_agree():
             a_u.copy_(a)
             t_u, i_u = flux.heads_to_tokens(a_u, S_txt)
             assert torch.equal(t_out, t_u) and torch.equal(i_out, i_u)
+            # image tokens into the first columns of a wider buffer
+            wide = torch.full((B, S_img, H * D + 64), 3.0, dtype=torch.bfloat16, device=dev)
+            _, i_w = flux.heads_to_tokens(a, S_txt, wide[..., :H * D])
+            assert torch.equal(i_w, i_out) and (wide[..., H * D:] == 3.0).all()
 
 
 def test_adaln_glue_matches_tensor_ops():

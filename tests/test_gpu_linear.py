@@ -323,3 +323,33 @@ def test_plan_choice(ops):
 
 def test_no_kernel_error_recorded(ops):
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("fmt", ["nf4", "fp8"])
+@pytest.mark.parametrize("mode,splits,m", [(0, 0, 4),      # small-M kernel
+                                           (1, 0, 300),    # fused one-CTA tiles
+                                           (2, 0, 300),    # fused CTA pairs
+                                           (1, 3, 16),     # split-K + reduce
+                                           (3, 0, 1100)])  # two-phase
+def test_output_into_column_range(ops, fmt, mode, splits, m):
+    # dq_linear_*_ld: y lands in columns [c0, c0 + N) of a wider row-major
+    # buffer, bit-identical to the plain call, with the other columns untouched
+    n, k, c0, width = 640, 1024, 256, 1280
+    x, w, bias, _ = _case(m, n, k, 41 + m, fmt, with_bias=True)
+    xc, bc = x.cuda(), bias.cuda()
+    ops.set_pair_mode(mode)
+    ops.set_tile_override(0, splits)
+    try:
+        buf = torch.full((m, width), 7.0, dtype=torch.bfloat16, device="cuda")
+        if fmt == "nf4":
+            plain = ops.nf4_linear(xc, w[0], w[1], n, bc, act="gelu_tanh")
+            ops.nf4_linear(xc, w[0], w[1], n, bc, act="gelu_tanh", out=buf[:, c0:c0 + n])
+        else:
+            plain = ops.fp8_linear(xc, w[0], w[1], bc, act="gelu_tanh")
+            ops.fp8_linear(xc, w[0], w[1], bc, act="gelu_tanh", out=buf[:, c0:c0 + n])
+        torch.cuda.synchronize()
+    finally:
+        ops.set_tile_override(0, 0)
+        ops.set_pair_mode(0)
+    assert torch.equal(buf[:, c0:c0 + n], plain)
+    assert (buf[:, :c0] == 7.0).all() and (buf[:, c0 + n:] == 7.0).all()
