@@ -98,3 +98,23 @@ def test_plan_info_rejects_bad_arguments_on_host(lib):
     assert lib.dq_plan_info(0, 8, 64, 0, *refs) == 1       # empty batch has no plan
     assert lib.dq_plan_info(4, 8, 64, 5, *refs) == 1       # unknown format
     assert lib.dq_plan_info(4, 8, 64, 0, None, *refs[1:]) == 7
+
+
+def test_strided_and_glue_entry_points_reject_bad_arguments_on_host(lib):
+    # validation happens before any CUDA call, so no GPU is needed to see it
+    p = ctypes.c_void_p(0x1000)
+    # y row stride below N
+    assert lib.dq_linear_nf4_ld(p, 4, 64, p, p, None, 64, 0, p, 32, None, 0, None) == 1
+    assert lib.dq_linear_fp8_ld(p, 4, 64, p, ctypes.c_float(1.0), None, 64, 0, p, 63, None, 0,
+                                None) == 1
+    # heads_to_tokens: output rows narrower than H * D
+    assert lib.dq_heads_to_tokens_ld(p, 1, 2, 0, 4, 64, None, 128, p, 100, None) == 1
+    # AdaLN modulation: D % 4, D above 8192, T not a multiple of S, NULL scale
+    assert lib.dq_adaln_modulate(p, 6, 4, 2, 6, p, p, 6, ctypes.c_float(1e-6), p, 6, None) == 1
+    assert lib.dq_adaln_modulate(p, 8196, 4, 2, 8196, p, p, 8196, ctypes.c_float(1e-6), p, 8196,
+                                 None) == 1
+    assert lib.dq_adaln_modulate(p, 8, 5, 2, 8, p, p, 8, ctypes.c_float(1e-6), p, 8, None) == 1
+    assert lib.dq_adaln_modulate(p, 8, 4, 2, 8, None, p, 8, ctypes.c_float(1e-6), p, 8, None) == 7
+    # gated residual: row stride below D, misaligned rows
+    assert lib.dq_gated_residual(p, 4, p, 8, p, 8, 4, 2, 8, p, 8, None) == 1
+    assert lib.dq_gated_residual(ctypes.c_void_p(0x1002), 8, p, 8, p, 8, 4, 2, 8, p, 8, None) == 2
