@@ -206,8 +206,8 @@ int dq_linear_fp8_ld(const void* x, int64_t M, int64_t K, const uint8_t* w8, flo
 
 /* Describes the launch plan dq_linear_* uses for this shape on the current
  * device: *pair = 0 for fused one-CTA tiles (128 weight rows), 1 for fused
- * CTA-pair tiles (256 rows), 2 for the two-phase plan (dequantize, then the
- * bf16 pair GEMM), 3 for the small-M kernel (*bm = 8 or 16 tokens, 16, 32 or
+ * CTA-pair tiles (256 rows), 2 for the two-phase plan (the bf16 CTA-pair GEMM
+ * whose launch also dequantizes the weight into scratch), 3 for the small-M kernel (*bm = 8 or 16 tokens, 16, 32 or
  * 64 weight rows per CTA); *bm = x-tile rows, *splits = split-K count, *grid = CTAs
  * launched.  A diagnostic query with no reference counterpart. */
 int dq_plan_info(int64_t M, int64_t N, int64_t K, int fmt, int* pair, int* bm, int* splits,
