@@ -86,7 +86,8 @@ int dq_dequant_fp8(const uint8_t* w8, float scale, int64_t n_elems,
  * partial sums for small token counts; for the two-phase plan of large ones
  * the bf16 weight (N*K*2, rounded up to 256) followed by the weight groups'
  * ready counters (4 * (N/256 + 2) bytes, rounded up to 256); else 0.  The
- * contents need no initialization. */
+ * contents need no initialization; calls that may run concurrently (on
+ * different streams) need distinct workspaces. */
 size_t dq_workspace_size(int64_t M, int64_t N, int64_t K, int fmt);
 
 /* y = x . dequant(W)^T + bias, dequantization fused into a tcgen05 GEMM.
