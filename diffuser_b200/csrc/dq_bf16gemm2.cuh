@@ -73,71 +73,19 @@ struct Bf16PairCfg {
 };
 
 // Decode weight rows [r0, r1) of the flat packed weight into dq_out: the
-// calling thread's share (thread tid of nthr) of the 16-byte chunks, four
-// chunks in flight per thread.
+// calling thread's share (thread tid of nthr) of the 16-byte chunks.
 template <int FMT>
 __device__ __forceinline__ void dequant_rows(const GemmArgs& a, int64_t r0, int64_t r1, int tid,
                                              int nthr) {
   const int64_t K = a.K;
   if constexpr (FMT == kFmtNF4) {
-    // 32 weights per chunk; block scale c >> 1
-    const uint4* src = reinterpret_cast<const uint4*>(a.dq_w);
-    uint4* dst = reinterpret_cast<uint4*>(a.dq_out);
-    const int64_t c1 = r1 * K / 32;
-    for (int64_t c = r0 * K / 32 + tid; c < c1; c += 4ll * nthr) {
-      uint4 p[4];
-      float am[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int64_t cu = c + static_cast<int64_t>(u) * nthr;
-        if (cu < c1) {
-          p[u] = __ldg(src + cu);
-          am[u] = __ldg(a.absmax + (cu >> 1));
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int64_t cu = c + static_cast<int64_t>(u) * nthr;
-        if (cu < c1) {
-          const Nf4Planes planes = nf4_scaled_planes(nf4_scale2(am[u]));
-          uint32_t o[16];
-          nf4_decode_word(p[u].x, planes, o + 0);
-          nf4_decode_word(p[u].y, planes, o + 4);
-          nf4_decode_word(p[u].z, planes, o + 8);
-          nf4_decode_word(p[u].w, planes, o + 12);
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            dst[4 * cu + j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
-        }
-      }
-    }
+    dequant_nf4_chunks(reinterpret_cast<const uint4*>(a.dq_w), a.absmax,
+                       reinterpret_cast<uint4*>(a.dq_out), r0 * K / 32, r1 * K / 32, tid, nthr);
   } else {
-    // 16 weights per chunk (K % 16 == 0, so rows hold whole chunks)
-    const float s = __bfloat162float(__float2bfloat16_rn(a.fp8_scale));
-    const uint4* src = reinterpret_cast<const uint4*>(a.dq_w);
-    uint4* dst = reinterpret_cast<uint4*>(a.dq_out);
-    const int64_t c1 = r1 * K / 16;
-    for (int64_t c = r0 * K / 16 + tid; c < c1; c += 4ll * nthr) {
-      uint4 p[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int64_t cu = c + static_cast<int64_t>(u) * nthr;
-        if (cu < c1) p[u] = __ldg(src + cu);
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int64_t cu = c + static_cast<int64_t>(u) * nthr;
-        if (cu < c1) {
-          uint32_t o[8];
-          fp8_decode_word(p[u].x, s, o + 0);
-          fp8_decode_word(p[u].y, s, o + 2);
-          fp8_decode_word(p[u].z, s, o + 4);
-          fp8_decode_word(p[u].w, s, o + 6);
-          dst[2 * cu] = make_uint4(o[0], o[1], o[2], o[3]);
-          dst[2 * cu + 1] = make_uint4(o[4], o[5], o[6], o[7]);
-        }
-      }
-    }
+    // K % 16 == 0, so rows hold whole chunks
+    dequant_fp8_chunks(reinterpret_cast<const uint4*>(a.dq_w),
+                       __bfloat162float(__float2bfloat16_rn(a.fp8_scale)),
+                       reinterpret_cast<uint4*>(a.dq_out), r0 * K / 16, r1 * K / 16, tid, nthr);
   }
 }
 

@@ -25,47 +25,131 @@
 namespace dq {
 
 // ------------------------------------------------------- standalone kernels
-// NF4 -> bf16: one thread per 16 packed bytes (32 elements of one block).
-__global__ void dequant_nf4_kernel(const uint4* __restrict__ packed, const float* __restrict__ absmax,
-                                   uint4* __restrict__ out, int64_t n_chunks) {
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n_chunks;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const uint4 p = __ldg(packed + i);
-    const Nf4Planes planes = nf4_scaled_planes(nf4_scale2(__ldg(absmax + (i >> 1))));
-    uint32_t o[16];
-    nf4_decode_word(p.x, planes, o + 0);
-    nf4_decode_word(p.y, planes, o + 4);
-    nf4_decode_word(p.z, planes, o + 8);
-    nf4_decode_word(p.w, planes, o + 12);
-    uint4* dst = out + 4 * i;
+// NF4 -> bf16: 16 packed bytes (32 weights of one block) per chunk, four
+// chunks in flight per thread.  A warp's 32 consecutive chunks decode to 2 KB
+// of contiguous output, staged through shared memory (16-byte pieces, XOR-
+// swizzled) so that each store instruction writes 512 contiguous bytes.
+__global__ void __launch_bounds__(256)
+    dequant_nf4_kernel(const uint4* __restrict__ packed, const float* __restrict__ absmax,
+                       uint4* __restrict__ out, int64_t n_chunks) {
+  __shared__ uint4 stage[8][128];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c - lane < n_chunks;
+       c += 4 * nthr) {
+    uint4 p[4];
+    float am[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) dst[j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+    for (int u = 0; u < 4; ++u) {
+      const int64_t cu = c + u * nthr;
+      if (cu < n_chunks) {
+        p[u] = __ldg(packed + cu);
+        am[u] = __ldg(absmax + (cu >> 1));
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t cu = c + u * nthr;
+      const int64_t cbase = cu - lane;  // the warp's first chunk (lanes are consecutive)
+      if (cbase >= n_chunks) break;      // warp-uniform
+      uint32_t o[16];
+      if (cu < n_chunks) {
+        const Nf4Planes planes = nf4_scaled_planes(nf4_scale2(am[u]));
+        nf4_decode_word(p[u].x, planes, o + 0);
+        nf4_decode_word(p[u].y, planes, o + 4);
+        nf4_decode_word(p[u].z, planes, o + 8);
+        nf4_decode_word(p[u].w, planes, o + 12);
+      }
+      if (cbase + 31 < n_chunks) {
+        // piece j of chunk q lives at stage[q * 4 + (j ^ (q & 3))]
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          stage[warp][lane * 4 + (j ^ (lane & 3))] =
+              make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int e = 32 * j + lane;  // 16-byte piece e of the warp's 2 KB
+          const int q = e >> 2;
+          out[4 * cbase + e] = stage[warp][q * 4 + ((e & 3) ^ (q & 3))];
+        }
+      } else if (cu < n_chunks) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          out[4 * cu + j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+      }
+    }
   }
 }
 
-// e4m3 -> bf16: 16 bytes per thread on the aligned body, scalar tail.
-__global__ void dequant_fp8_kernel(const uint8_t* __restrict__ w8, float scale,
-                                   __nv_bfloat16* __restrict__ out, int64_t n) {
+// e4m3 -> bf16: 16 bytes per chunk on the aligned body (four chunks in
+// flight per thread; a warp's 32 chunks decode to 1 KB of contiguous output,
+// staged through shared memory so that each store instruction writes 512
+// contiguous bytes), scalar tail.
+__global__ void __launch_bounds__(256)
+    dequant_fp8_kernel(const uint8_t* __restrict__ w8, float scale, __nv_bfloat16* __restrict__ out,
+                       int64_t n) {
+  __shared__ uint4 stage[8][64];
   const float s = __bfloat162float(__float2bfloat16_rn(scale));
   const int64_t n16 = n / 16;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
   const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   const int64_t nth = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = tid; i < n16; i += nth) {
-    const uint4 p = __ldg(reinterpret_cast<const uint4*>(w8) + i);
-    uint32_t o[8];
-    fp8_decode_word(p.x, s, o + 0);
-    fp8_decode_word(p.y, s, o + 2);
-    fp8_decode_word(p.z, s, o + 4);
-    fp8_decode_word(p.w, s, o + 6);
-    uint4* dst = reinterpret_cast<uint4*>(out) + 2 * i;
-    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  const uint4* src = reinterpret_cast<const uint4*>(w8);
+  uint4* dst = reinterpret_cast<uint4*>(out);
+  for (int64_t c = tid; c - lane < n16; c += 4 * nth) {
+    uint4 p[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t cu = c + u * nth;
+      if (cu < n16) p[u] = __ldg(src + cu);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t cu = c + u * nth;
+      const int64_t cbase = cu - lane;  // the warp's first chunk
+      if (cbase >= n16) break;           // warp-uniform
+      uint32_t o[8];
+      if (cu < n16) {
+        fp8_decode_word(p[u].x, s, o + 0);
+        fp8_decode_word(p[u].y, s, o + 2);
+        fp8_decode_word(p[u].z, s, o + 4);
+        fp8_decode_word(p[u].w, s, o + 6);
+      }
+      if (cbase + 31 < n16) {
+        // piece j of chunk q lives at stage[q * 2 + (j ^ (q & 1))]
+        __syncwarp();
+        stage[warp][lane * 2 + (lane & 1)] = make_uint4(o[0], o[1], o[2], o[3]);
+        stage[warp][lane * 2 + (1 ^ (lane & 1))] = make_uint4(o[4], o[5], o[6], o[7]);
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int e = 32 * j + lane;  // 16-byte piece e of the warp's 1 KB
+          const int q = e >> 1;
+          dst[2 * cbase + e] = stage[warp][q * 2 + ((e & 1) ^ (q & 1))];
+        }
+      } else if (cu < n16) {
+        dst[2 * cu] = make_uint4(o[0], o[1], o[2], o[3]);
+        dst[2 * cu + 1] = make_uint4(o[4], o[5], o[6], o[7]);
+      }
+    }
   }
   for (int64_t i = n16 * 16 + tid; i < n; i += nth) {
     uint32_t o[2];
     fp8_decode_word(static_cast<uint32_t>(w8[i]), s, o);
     out[i] = __ushort_as_bfloat16(static_cast<unsigned short>(o[0] & 0xFFFFu));
   }
+}
+
+// Grid of an elementwise decode: four chunks per thread per pass, at most the
+// CTAs that are resident at once (8 x 256 threads per SM).
+static int decode_grid(int64_t chunks, int sms) {
+  int64_t g = (chunks + 4 * 256 - 1) / (4 * 256);
+  g = std::min<int64_t>(g, static_cast<int64_t>(sms) * 8);
+  return static_cast<int>(std::max<int64_t>(g, 1));
 }
 
 template <typename T>
@@ -690,10 +774,10 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
     if (separate) {
       const int64_t n_elems = N * K;
       if (fmt == kFmtNF4) {
-        dequant_nf4_kernel<<<grid_for(n_elems / 32, 256, d->sms), 256, 0, st>>>(
+        dequant_nf4_kernel<<<decode_grid(n_elems / 32, d->sms), 256, 0, st>>>(
             reinterpret_cast<const uint4*>(w), absmax, static_cast<uint4*>(ws), n_elems / 32);
       } else {
-        dequant_fp8_kernel<<<grid_for(n_elems / 16 + 1, 256, d->sms), 256, 0, st>>>(
+        dequant_fp8_kernel<<<decode_grid(n_elems / 16 + 1, d->sms), 256, 0, st>>>(
             w, scale, static_cast<__nv_bfloat16*>(ws), n_elems);
       }
       if (cudaGetLastError() != cudaSuccess) return DQ_ERR_LAUNCH;
@@ -936,7 +1020,7 @@ int dq_dequant_nf4(const uint8_t* packed, const float* absmax, int64_t n_elems, 
   int rc = current_device(&d);
   if (rc != DQ_OK) return rc;
   const int64_t chunks = n_elems / 32;
-  dequant_nf4_kernel<<<grid_for(chunks, 256, d->sms), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  dequant_nf4_kernel<<<decode_grid(chunks, d->sms), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const uint4*>(packed), absmax, static_cast<uint4*>(out_bf16), chunks);
   return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
 }
@@ -950,7 +1034,7 @@ int dq_dequant_fp8(const uint8_t* w8, float scale, int64_t n_elems, void* out_bf
   DeviceInfo* d = nullptr;
   int rc = current_device(&d);
   if (rc != DQ_OK) return rc;
-  dequant_fp8_kernel<<<grid_for(n_elems / 16 + 1, 256, d->sms), 256, 0,
+  dequant_fp8_kernel<<<decode_grid(n_elems / 16 + 1, d->sms), 256, 0,
                        static_cast<cudaStream_t>(stream)>>>(w8, scale,
                                                             static_cast<__nv_bfloat16*>(out_bf16), n_elems);
   return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;

@@ -201,6 +201,70 @@ __device__ __forceinline__ uint8_t f32_to_e4m3(float v) {
 }
 
 // ------------------------------------------------------------ activation
+// Decode 16-byte chunks c0 + tid, c0 + tid + nthr, ... (< c1) of a flat
+// packed weight into bf16, four chunks in flight per thread (the loads of
+// all four are issued before any is decoded).  NF4: a chunk is 32 weights of
+// one 64-block (block scale index c >> 1), written as 4 x 16 bytes; fp8: 16
+// weights times the bf16-rounded scale s, written as 2 x 16 bytes.
+__device__ __forceinline__ void dequant_nf4_chunks(const uint4* __restrict__ src,
+                                                   const float* __restrict__ absmax,
+                                                   uint4* __restrict__ dst, int64_t c0, int64_t c1,
+                                                   int64_t tid, int64_t nthr) {
+  for (int64_t c = c0 + tid; c < c1; c += 4 * nthr) {
+    uint4 p[4];
+    float am[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t cu = c + u * nthr;
+      if (cu < c1) {
+        p[u] = __ldg(src + cu);
+        am[u] = __ldg(absmax + (cu >> 1));
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t cu = c + u * nthr;
+      if (cu < c1) {
+        const Nf4Planes planes = nf4_scaled_planes(nf4_scale2(am[u]));
+        uint32_t o[16];
+        nf4_decode_word(p[u].x, planes, o + 0);
+        nf4_decode_word(p[u].y, planes, o + 4);
+        nf4_decode_word(p[u].z, planes, o + 8);
+        nf4_decode_word(p[u].w, planes, o + 12);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          dst[4 * cu + j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void dequant_fp8_chunks(const uint4* __restrict__ src, float s,
+                                                   uint4* __restrict__ dst, int64_t c0, int64_t c1,
+                                                   int64_t tid, int64_t nthr) {
+  for (int64_t c = c0 + tid; c < c1; c += 4 * nthr) {
+    uint4 p[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t cu = c + u * nthr;
+      if (cu < c1) p[u] = __ldg(src + cu);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t cu = c + u * nthr;
+      if (cu < c1) {
+        uint32_t o[8];
+        fp8_decode_word(p[u].x, s, o + 0);
+        fp8_decode_word(p[u].y, s, o + 2);
+        fp8_decode_word(p[u].z, s, o + 4);
+        fp8_decode_word(p[u].w, s, o + 6);
+        dst[2 * cu] = make_uint4(o[0], o[1], o[2], o[3]);
+        dst[2 * cu + 1] = make_uint4(o[4], o[5], o[6], o[7]);
+      }
+    }
+  }
+}
+
 enum : int { kActNone = 0, kActGeluTanh = 1 };
 
 // GELU, tanh approximation, in float32: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))),
