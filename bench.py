@@ -53,7 +53,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["tp_fp8", "flux_dit", "small_nf4", "small_fp8"],
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["tp_fp8", "flux_dit", "small_nf4", "small_fp8",
+                                                           "dequant_nf4", "dequant_fp8"],
                     default="nf4")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -910,11 +911,132 @@ def run_small(args, world, rank, local):
         dist.destroy_process_group()
 
 
+# ------------------------------------------------------ standalone decode
+def run_dequant(args, world, rank, local):
+    """The standalone dequantization (ltx23_nf4_dequantize, R/nf4_ltx23.R:
+    77-115; the fp8 upcast x scale, R/fp8_ltx23.R:79-80) of the 12288 x 3072
+    weight into bf16, over 4 rotating weight / output sets (387 MB NF4): HBM-
+    bound, value = GB/s of packed + scales read and bf16 written."""
+    from diffuser_b200 import ops
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    fmt = args.workload.split("_")[1]
+    stream = torch.cuda.current_stream(dev)
+    g0 = torch.Generator(device=dev).manual_seed(0)
+    w = torch.randn(N, K, generator=g0, device=dev) * 0.02
+    outs = [torch.empty(N, K, dtype=torch.bfloat16, device=dev) for _ in range(ROTATE)]
+    if fmt == "nf4":
+        p0, a0 = ops.ltx23_nf4_quantize(w)
+        sets = [(p0.clone(), a0.clone()) for _ in range(ROTATE)]
+        byts = N * K // 2 + N * K // 64 * 4 + N * K * 2
+        call = lambda i: ops.ltx23_nf4_dequantize(*sets[i % ROTATE], (N, K), out=outs[i % ROTATE])
+    else:
+        w80, s0 = ops.fp8_quantize(w)
+        scale = float(s0.item())
+        sets = [w80.clone() for _ in range(ROTATE)]
+        byts = N * K + N * K * 2
+        call = lambda i: ops.fp8_dequantize(sets[i % ROTATE], scale, out=outs[i % ROTATE])
+    del w
+    for i in range(max(args.warmup, 3)):
+        call(i)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        a.record(stream)
+        for i in range(args.steps):
+            call(i)
+        b.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    us = max_over_ranks(a.elapsed_time(b) * 1e3 / args.steps, world, dev)
+    err = ops.device_error(dev)
+    if err != 0:
+        raise RuntimeError(f"kernel error word {err}")
+    # end to end through the public op: packed weight up, bf16 weight down
+    e2e = None
+    if not args.no_e2e:
+        if fmt == "nf4":
+            hp, ha = sets[0][0].cpu().pin_memory(), sets[0][1].cpu().pin_memory()
+            dp, da = torch.empty_like(sets[0][0]), torch.empty_like(sets[0][1])
+            h2d = hp.numel() + ha.numel() * 4
+        else:
+            hp = sets[0].view(torch.uint8).cpu().pin_memory()
+            dp = torch.empty_like(sets[0].view(torch.uint8))
+            h2d = hp.numel()
+        hw = torch.empty(N, K, dtype=torch.bfloat16).pin_memory()
+
+        def e2e_step():
+            dp.copy_(hp, non_blocking=True)
+            if fmt == "nf4":
+                da.copy_(ha, non_blocking=True)
+                wb = ops.ltx23_nf4_dequantize(dp, da, (N, K), out=outs[0])
+            else:
+                wb = ops.fp8_dequantize(dp.view(torch.float8_e4m3fn), scale, out=outs[0])
+            hw.copy_(wb, non_blocking=True)
+
+        n_e2e = max(5, min(args.steps, 20))
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        a.record(stream)
+        for _ in range(n_e2e):
+            e2e_step()
+        b.record(stream)
+        torch.cuda.synchronize()
+        e_us = max_over_ranks(a.elapsed_time(b) * 1e3 / n_e2e, world, dev)
+        e2e = {"value": world * byts / e_us / 1e3, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": N * K * 2, "us_per_step": e_us,
+               "api": f"diffuser_b200.ops.{'ltx23_nf4_dequantize' if fmt == 'nf4' else 'fp8_dequantize'}"}
+    # the reference's GPU op sequence for the same decode
+    ref_us = None
+    if world == 1:
+        rdq = RefGpuDequant(dev)
+        ref = (lambda i: rdq.nf4(*sets[i % ROTATE], N, K)) if fmt == "nf4" else \
+            (lambda i: rdq.fp8(sets[i % ROTATE].view(torch.uint8), scale))
+        for i in range(3):
+            ref(i)
+        torch.cuda.synchronize()
+        a.record(stream)
+        for i in range(20):
+            ref(i)
+        b.record(stream)
+        torch.cuda.synchronize()
+        ref_us = a.elapsed_time(b) * 1e3 / 20
+        del rdq
+    if rank == 0:
+        _, _, hbm, peak_src = measured_peaks()
+        gbs = byts / us / 1e3
+        line = {
+            "metric": f"{fmt.upper()} dequantize GB/s ({N}x{K} -> bf16)", "value": world * gbs,
+            "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": us / 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u8" if fmt == "nf4" else "fp8", "data": "synthetic",
+            "config": {"workload": f"{'ltx23_nf4_dequantize' if fmt == 'nf4' else 'fp8 upcast x scale'} "
+                                   f"W[{N},{K}] -> bf16", "parallelism": f"dp{world} (replicas)",
+                       "l2": f"{ROTATE} rotating weight / output sets ({ROTATE * byts / 1e6:.0f} MB) > 126 MB L2"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                         "traffic": None, "peak_source": f"{peak_src} HBM copy bandwidth",
+                         "kernel": f"dequant_{fmt}_kernel", "algorithmic_bytes": byts},
+            "reference_gpu_algorithm_us": ref_us,
+            "speedup_vs_reference_gpu_algorithm": (ref_us / us) if ref_us else None,
+            "cpu_baseline": None, "e2e": e2e, "gpu_launches": args.steps, "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
-        if args.workload in ("tp_fp8", "flux_dit", "small_nf4", "small_fp8"):
+        if args.workload in ("tp_fp8", "flux_dit", "small_nf4", "small_fp8", "dequant_nf4", "dequant_fp8"):
             if rank == 0:
                 why = ("the reference runs each linear on one GPU; it has no column-parallel path"
                        if args.workload == "tp_fp8" else
@@ -922,7 +1044,10 @@ def main():
                        "is timed inside the flux_dit line (reference_algorithm_step_ms)"
                        if args.workload == "flux_dit" else
                        "the small-M sweep times the reference's GPU algorithm at M = 1 inside its own line "
-                       "(reference_gpu_algorithm_us_M1); the CPU reference arm runs on the default workload")
+                       "(reference_gpu_algorithm_us_M1); the CPU reference arm runs on the default workload"
+                       if args.workload.startswith("small_") else
+                       "the decode line times the reference's GPU op sequence inside its own line "
+                       "(reference_gpu_algorithm_us); the CPU reference arm runs on the default workload")
                 print(json.dumps({"impl": "reference", "unavailable": why}))
             return
         run_reference_arm(args, world, rank)
@@ -935,6 +1060,9 @@ def main():
         return
     if args.workload.startswith("small_"):
         run_small(args, world, rank, local)
+        return
+    if args.workload.startswith("dequant_"):
+        run_dequant(args, world, rank, local)
         return
     run_ours(args, world, rank, local)
 
