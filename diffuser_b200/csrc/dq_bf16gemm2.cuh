@@ -46,7 +46,8 @@ struct Bf16PairCfg {
   static constexpr int kXStageBytes = kHalfBM * 128;
   static constexpr int kEpiWarps = 8;
   static constexpr int kEpiCols = 32;
-  static constexpr int kEpiBytes = kEpiWarps * kEpiCols * 32 * 4;
+  static constexpr int kEpiWarpBytes = kEpiCols * 32 * 2;  // [32 tokens][32 outputs] bf16
+  static constexpr int kEpiBytes = kEpiWarps * kEpiWarpBytes;
   static constexpr int kSmemLimit = 227 * 1024;
   static constexpr int kStagesFit =
       (kSmemLimit - kEpiBytes - 2048 - 1024) / (kAStageBytes + kXStageBytes);
@@ -76,16 +77,18 @@ struct Bf16PairCfg {
 // calling thread's share (thread tid of nthr) of the 16-byte chunks.
 template <int FMT>
 __device__ __forceinline__ void dequant_rows(const GemmArgs& a, int64_t r0, int64_t r1, int tid,
-                                             int nthr) {
+                                             int nthr, uint4* stage) {
   const int64_t K = a.K;
   if constexpr (FMT == kFmtNF4) {
     dequant_nf4_chunks(reinterpret_cast<const uint4*>(a.dq_w), a.absmax,
-                       reinterpret_cast<uint4*>(a.dq_out), r0 * K / 32, r1 * K / 32, tid, nthr);
+                       reinterpret_cast<uint4*>(a.dq_out), r0 * K / 32, r1 * K / 32, tid, nthr,
+                       stage);
   } else {
     // K % 16 == 0, so rows hold whole chunks
     dequant_fp8_chunks(reinterpret_cast<const uint4*>(a.dq_w),
                        __bfloat162float(__float2bfloat16_rn(a.fp8_scale)),
-                       reinterpret_cast<uint4*>(a.dq_out), r0 * K / 16, r1 * K / 16, tid, nthr);
+                       reinterpret_cast<uint4*>(a.dq_out), r0 * K / 16, r1 * K / 16, tid, nthr,
+                       stage);
   }
 }
 
@@ -237,7 +240,9 @@ __global__ void __launch_bounds__(Bf16PairCfg<BM, FMT>::kThreads, 1)
         const int gn = g == 0 ? g0 : min(args.group_n, args.num_n_tiles - nb);
         const int64_t r0 = static_cast<int64_t>(nb) * 256;
         const int64_t r1 = min(static_cast<int64_t>(args.N), static_cast<int64_t>(nb + gn) * 256);
-        dequant_rows<FMT>(args, r0, r1, tid, nthr);
+        // stores go out directly: staging them through shared memory (as the
+        // standalone decode does) measured no faster beside the GEMM
+        dequant_rows<FMT>(args, r0, r1, tid, nthr, nullptr);
         // every lane's stores, then the warp's count (release)
         fence_proxy_async_global();
         __threadfence();
@@ -252,8 +257,8 @@ __global__ void __launch_bounds__(Bf16PairCfg<BM, FMT>::kThreads, 1)
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int half = warp >> 2;  // which half of the tile's columns it drains
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
-    uint8_t* stg = smem + C::kOffEpi + warp * (EC * 32 * 4);
-    const uint32_t stg_s = sbase + C::kOffEpi + warp * (EC * 32 * 4);
+    uint8_t* stg = smem + C::kOffEpi + warp * C::kEpiWarpBytes;
+    const uint32_t stg_s = sbase + C::kOffEpi + warp * C::kEpiWarpBytes;
     int acc = 0;
     uint32_t accphase = 0;
     for (int t = pair; t < args.num_tiles; t += npairs) {

@@ -25,118 +25,28 @@
 namespace dq {
 
 // ------------------------------------------------------- standalone kernels
-// NF4 -> bf16: 16 packed bytes (32 weights of one block) per chunk, four
-// chunks in flight per thread.  A warp's 32 consecutive chunks decode to 2 KB
-// of contiguous output, staged through shared memory (16-byte pieces, XOR-
-// swizzled) so that each store instruction writes 512 contiguous bytes.
+// NF4 -> bf16 and e4m3 -> bf16 over the whole flat weight (the staged chunk
+// loops of dq_codec.cuh; 8 warps x 2 KB of staging per CTA), fp8 with a
+// scalar tail for n % 16.
 __global__ void __launch_bounds__(256)
     dequant_nf4_kernel(const uint4* __restrict__ packed, const float* __restrict__ absmax,
                        uint4* __restrict__ out, int64_t n_chunks) {
   __shared__ uint4 stage[8][128];
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c - lane < n_chunks;
-       c += 4 * nthr) {
-    uint4 p[4];
-    float am[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int64_t cu = c + u * nthr;
-      if (cu < n_chunks) {
-        p[u] = __ldg(packed + cu);
-        am[u] = __ldg(absmax + (cu >> 1));
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int64_t cu = c + u * nthr;
-      const int64_t cbase = cu - lane;  // the warp's first chunk (lanes are consecutive)
-      if (cbase >= n_chunks) break;      // warp-uniform
-      uint32_t o[16];
-      if (cu < n_chunks) {
-        const Nf4Planes planes = nf4_scaled_planes(nf4_scale2(am[u]));
-        nf4_decode_word(p[u].x, planes, o + 0);
-        nf4_decode_word(p[u].y, planes, o + 4);
-        nf4_decode_word(p[u].z, planes, o + 8);
-        nf4_decode_word(p[u].w, planes, o + 12);
-      }
-      if (cbase + 31 < n_chunks) {
-        // piece j of chunk q lives at stage[q * 4 + (j ^ (q & 3))]
-        __syncwarp();
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          stage[warp][lane * 4 + (j ^ (lane & 3))] =
-              make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
-        __syncwarp();
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int e = 32 * j + lane;  // 16-byte piece e of the warp's 2 KB
-          const int q = e >> 2;
-          out[4 * cbase + e] = stage[warp][q * 4 + ((e & 3) ^ (q & 3))];
-        }
-      } else if (cu < n_chunks) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          out[4 * cu + j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
-      }
-    }
-  }
+  dequant_nf4_chunks(packed, absmax, out, 0, n_chunks,
+                     blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x,
+                     static_cast<int64_t>(gridDim.x) * blockDim.x, stage[threadIdx.x >> 5]);
 }
 
-// e4m3 -> bf16: 16 bytes per chunk on the aligned body (four chunks in
-// flight per thread; a warp's 32 chunks decode to 1 KB of contiguous output,
-// staged through shared memory so that each store instruction writes 512
-// contiguous bytes), scalar tail.
 __global__ void __launch_bounds__(256)
     dequant_fp8_kernel(const uint8_t* __restrict__ w8, float scale, __nv_bfloat16* __restrict__ out,
                        int64_t n) {
   __shared__ uint4 stage[8][64];
   const float s = __bfloat162float(__float2bfloat16_rn(scale));
   const int64_t n16 = n / 16;
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
   const int64_t tid = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   const int64_t nth = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  const uint4* src = reinterpret_cast<const uint4*>(w8);
-  uint4* dst = reinterpret_cast<uint4*>(out);
-  for (int64_t c = tid; c - lane < n16; c += 4 * nth) {
-    uint4 p[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int64_t cu = c + u * nth;
-      if (cu < n16) p[u] = __ldg(src + cu);
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int64_t cu = c + u * nth;
-      const int64_t cbase = cu - lane;  // the warp's first chunk
-      if (cbase >= n16) break;           // warp-uniform
-      uint32_t o[8];
-      if (cu < n16) {
-        fp8_decode_word(p[u].x, s, o + 0);
-        fp8_decode_word(p[u].y, s, o + 2);
-        fp8_decode_word(p[u].z, s, o + 4);
-        fp8_decode_word(p[u].w, s, o + 6);
-      }
-      if (cbase + 31 < n16) {
-        // piece j of chunk q lives at stage[q * 2 + (j ^ (q & 1))]
-        __syncwarp();
-        stage[warp][lane * 2 + (lane & 1)] = make_uint4(o[0], o[1], o[2], o[3]);
-        stage[warp][lane * 2 + (1 ^ (lane & 1))] = make_uint4(o[4], o[5], o[6], o[7]);
-        __syncwarp();
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int e = 32 * j + lane;  // 16-byte piece e of the warp's 1 KB
-          const int q = e >> 1;
-          dst[2 * cbase + e] = stage[warp][q * 2 + ((e & 1) ^ (q & 1))];
-        }
-      } else if (cu < n16) {
-        dst[2 * cu] = make_uint4(o[0], o[1], o[2], o[3]);
-        dst[2 * cu + 1] = make_uint4(o[4], o[5], o[6], o[7]);
-      }
-    }
-  }
+  dequant_fp8_chunks(reinterpret_cast<const uint4*>(w8), s, reinterpret_cast<uint4*>(out), 0, n16,
+                     tid, nth, stage[threadIdx.x >> 5]);
   for (int64_t i = n16 * 16 + tid; i < n; i += nth) {
     uint32_t o[2];
     fp8_decode_word(static_cast<uint32_t>(w8[i]), s, o);

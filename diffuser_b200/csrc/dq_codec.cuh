@@ -202,15 +202,23 @@ __device__ __forceinline__ uint8_t f32_to_e4m3(float v) {
 
 // ------------------------------------------------------------ activation
 // Decode 16-byte chunks c0 + tid, c0 + tid + nthr, ... (< c1) of a flat
-// packed weight into bf16, four chunks in flight per thread (the loads of
-// all four are issued before any is decoded).  NF4: a chunk is 32 weights of
-// one 64-block (block scale index c >> 1), written as 4 x 16 bytes; fp8: 16
-// weights times the bf16-rounded scale s, written as 2 x 16 bytes.
+// packed weight into bf16, four chunks in flight per thread (the loads of all
+// four are issued before any is decoded).  NF4: a chunk is 32 weights of one
+// 64-block (block scale index c >> 1) and decodes to 4 x 16 bytes; fp8: 16
+// weights times the bf16-rounded scale s, 2 x 16 bytes.
+//
+// Called by whole warps whose lanes hold consecutive tids (tid % 32 == lane):
+// a warp's 32 consecutive chunks decode to one contiguous run (2 KB NF4, 1 KB
+// fp8), which goes through `stage` (the warp's own 128 / 64 x 16 bytes of
+// shared memory, XOR-swizzled) so that each store instruction writes 512
+// contiguous bytes; a warp whose 32 chunks straddle c1, or one given no stage
+// (nullptr), stores each chunk directly.
 __device__ __forceinline__ void dequant_nf4_chunks(const uint4* __restrict__ src,
                                                    const float* __restrict__ absmax,
                                                    uint4* __restrict__ dst, int64_t c0, int64_t c1,
-                                                   int64_t tid, int64_t nthr) {
-  for (int64_t c = c0 + tid; c < c1; c += 4 * nthr) {
+                                                   int64_t tid, int64_t nthr, uint4* stage) {
+  const int lane = threadIdx.x & 31;
+  for (int64_t c = c0 + tid; c - lane < c1; c += 4 * nthr) {
     uint4 p[4];
     float am[4];
 #pragma unroll
@@ -224,13 +232,31 @@ __device__ __forceinline__ void dequant_nf4_chunks(const uint4* __restrict__ src
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int64_t cu = c + u * nthr;
+      const int64_t cbase = cu - lane;  // the warp's first chunk
+      if (cbase >= c1) break;            // warp-uniform
+      uint32_t o[16];
       if (cu < c1) {
         const Nf4Planes planes = nf4_scaled_planes(nf4_scale2(am[u]));
-        uint32_t o[16];
         nf4_decode_word(p[u].x, planes, o + 0);
         nf4_decode_word(p[u].y, planes, o + 4);
         nf4_decode_word(p[u].z, planes, o + 8);
         nf4_decode_word(p[u].w, planes, o + 12);
+      }
+      if (stage != nullptr && cbase + 31 < c1) {
+        // piece j of chunk q lives at stage[q * 4 + (j ^ (q & 3))]
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          stage[lane * 4 + (j ^ (lane & 3))] =
+              make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int e = 32 * j + lane;  // 16-byte piece e of the warp's 2 KB
+          const int q = e >> 2;
+          dst[4 * cbase + e] = stage[q * 4 + ((e & 3) ^ (q & 3))];
+        }
+      } else if (cu < c1) {
 #pragma unroll
         for (int j = 0; j < 4; ++j)
           dst[4 * cu + j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
@@ -241,8 +267,9 @@ __device__ __forceinline__ void dequant_nf4_chunks(const uint4* __restrict__ src
 
 __device__ __forceinline__ void dequant_fp8_chunks(const uint4* __restrict__ src, float s,
                                                    uint4* __restrict__ dst, int64_t c0, int64_t c1,
-                                                   int64_t tid, int64_t nthr) {
-  for (int64_t c = c0 + tid; c < c1; c += 4 * nthr) {
+                                                   int64_t tid, int64_t nthr, uint4* stage) {
+  const int lane = threadIdx.x & 31;
+  for (int64_t c = c0 + tid; c - lane < c1; c += 4 * nthr) {
     uint4 p[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
@@ -252,12 +279,28 @@ __device__ __forceinline__ void dequant_fp8_chunks(const uint4* __restrict__ src
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int64_t cu = c + u * nthr;
+      const int64_t cbase = cu - lane;
+      if (cbase >= c1) break;  // warp-uniform
+      uint32_t o[8];
       if (cu < c1) {
-        uint32_t o[8];
         fp8_decode_word(p[u].x, s, o + 0);
         fp8_decode_word(p[u].y, s, o + 2);
         fp8_decode_word(p[u].z, s, o + 4);
         fp8_decode_word(p[u].w, s, o + 6);
+      }
+      if (stage != nullptr && cbase + 31 < c1) {
+        // piece j of chunk q lives at stage[q * 2 + (j ^ (q & 1))]
+        __syncwarp();
+        stage[lane * 2 + (lane & 1)] = make_uint4(o[0], o[1], o[2], o[3]);
+        stage[lane * 2 + (1 ^ (lane & 1))] = make_uint4(o[4], o[5], o[6], o[7]);
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int e = 32 * j + lane;  // 16-byte piece e of the warp's 1 KB
+          const int q = e >> 1;
+          dst[2 * cbase + e] = stage[q * 2 + ((e & 1) ^ (q & 1))];
+        }
+      } else if (cu < c1) {
         dst[2 * cu] = make_uint4(o[0], o[1], o[2], o[3]);
         dst[2 * cu + 1] = make_uint4(o[4], o[5], o[6], o[7]);
       }
