@@ -106,10 +106,10 @@ int dq_linear_fp8(const void* x, int64_t M, int64_t K,
                   void* workspace, size_t workspace_bytes, dq_stream_t stream);
 
 /* Allocation-free NF4 linear, for callers that cannot allocate device
- * memory: code running inside a CUDA graph capture or another runtime's
- * stream callbacks, and embedders whose device memory is owned by a foreign
- * allocator (the R torch package's caching allocator, for instance) and who
- * have no workspace to lend.  This entry point has no counterpart in the
+ * memory: embedders whose device memory is owned by a foreign allocator (the
+ * R torch package's caching allocator, for instance) and who have no
+ * workspace to lend, and code that must not allocate while it runs (a
+ * serving loop with a fixed memory budget).  This entry point has no counterpart in the
  * reference.  Same math and arguments as dq_linear_nf4 minus the workspace:
  * split-K partial sums go to a scratch array built into the library
  * (DQ_NOALLOC_SCRATCH_BYTES = 8 MiB, held on every GPU that loads the

@@ -1,7 +1,7 @@
 """dq_linear_nf4_noalloc: the NF4 linear for callers that cannot allocate device
-memory (code inside a CUDA graph capture, foreign runtimes' callbacks, or an
-embedder whose memory belongs to another allocator and who has no workspace to
-lend).  Its split-K scratch is an 8 MiB array built into the library.
+memory (an embedder whose memory belongs to another allocator and who has no
+workspace to lend, or code that must not allocate while it runs).  Its split-K
+scratch is an 8 MiB array built into the library.
 
 The test drives it through the C ABI (ctypes) and checks two consecutive calls
 against the workspace-taking dq_linear_nf4, within the linear tolerance used
