@@ -118,3 +118,17 @@ def test_strided_and_glue_entry_points_reject_bad_arguments_on_host(lib):
     # gated residual: row stride below D, misaligned rows
     assert lib.dq_gated_residual(p, 4, p, 8, p, 8, 4, 2, 8, p, 8, None) == 1
     assert lib.dq_gated_residual(ctypes.c_void_p(0x1002), 8, p, 8, p, 8, 4, 2, 8, p, 8, None) == 2
+
+
+def test_linear_out_argument_is_validated_on_host():
+    # out= must be a bf16 CUDA view with unit feature stride and evenly spaced
+    # rows; the checks run before any launch
+    import torch
+    from diffuser_b200 import ops
+    with pytest.raises(TypeError):
+        ops._out_rows(torch.empty(4, 8, dtype=torch.float32), 4, 8)
+    if torch.cuda.is_available():
+        return
+    # on a host without CUDA the device check is the first to refuse
+    with pytest.raises(TypeError):
+        ops._out_rows(torch.empty(4, 8, dtype=torch.bfloat16), 4, 8)
