@@ -6,6 +6,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdint>
 #include <atomic>
 #include <cstdio>
 #include <cstdlib>
@@ -287,9 +288,14 @@ static size_t twophase_counter_bytes(int n_tiles) {
 // group's bf16 weight stays in L2 while the token tiles sweep past it).
 constexpr int kTwoPhaseGroupN = 16;
 
+// max_split_ws: the most split-K scratch the caller can hold (the
+// allocation-free entry point's built-in array); plans needing more split only
+// where they always did.
 static Plan make_plan(int fmt, int64_t M, int64_t N, int64_t K, int sms, bool allow_split = true,
-                      bool allow_twophase = true, bool allow_smallm = true) {
+                      bool allow_twophase = true, bool allow_smallm = true,
+                      size_t max_split_ws = SIZE_MAX) {
   Plan p;
+  int long_k_split = 0;
   const int KB = static_cast<int>((K + 63) / 64);
   // 0 automatic, 1 one-CTA fused only, 2 CTA-pair fused only, 3 two-phase
   // only, 4 two-phase only with the dequantization as its own launch, 5 the
@@ -366,6 +372,26 @@ static Plan make_plan(int fmt, int64_t M, int64_t N, int64_t K, int sms, bool al
         p.bm = c.bm;
       }
     }
+    // Long K on a partial wave: one-CTA tiles split in two K halves that fill
+    // the SMs exactly once, costed at half a tile plus 15% for the f32 partials
+    // and their reduce (measured at M = 512, 12288 -> 3072: 192-row tiles split
+    // two ways 58.6 us against 75.2 for the unsplit 128-row grid; the
+    // 3072-deep projections of that size stay unsplit, as measured fastest).
+    if (allow_split && KB >= 128 && opair == 0 && obm == 0 && g_override_splits.load() == 0 &&
+        static_cast<size_t>(2) * M * N * sizeof(float) <= max_split_ws) {
+      for (const TileShape& c : kShapes) {
+        if (c.pair) continue;
+        const int64_t tiles = ((M + c.bm - 1) / c.bm) * n_tiles_of(false) * 2;
+        if (tiles > units_of(false)) continue;
+        const double cost = 1.15 * 128.0 * c.bm / c.eff / 2.0;
+        if (cost < best - 1e-9) {
+          best = cost;
+          p.pair = false;
+          p.bm = c.bm;
+          long_k_split = 2;
+        }
+      }
+    }
   }
   p.n_tiles = n_tiles_of(p.pair);
   const int units = units_of(p.pair);
@@ -375,6 +401,8 @@ static Plan make_plan(int fmt, int64_t M, int64_t N, int64_t K, int sms, bool al
   const int os = g_override_splits.load();
   if (os > 0) {
     s = os;
+  } else if (long_k_split > 0) {
+    s = long_k_split;
   } else if (allow_split && !p.twophase && base_tiles * 2 <= units && KB >= 8) {
     s = std::min(std::min(units / base_tiles, KB / 4), 16);
   }
@@ -642,7 +670,8 @@ static int launch_smallm(DeviceInfo* d, const Plan& p, const void* x, const uint
 static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8_t* w,
                        const float* absmax, float scale, const void* bias, int64_t N, void* y,
                        void* ws, size_t ws_bytes, cudaStream_t st, const TpOpts* tp = nullptr,
-                       bool allow_twophase = true, int act = kActNone, int64_t ldy = 0) {
+                       bool allow_twophase = true, int act = kActNone, int64_t ldy = 0,
+                       size_t max_split_ws = SIZE_MAX) {
   if (act != kActNone && act != kActGeluTanh) return DQ_ERR_ARG;
   // y row stride (elements): N unless the caller writes into a wider buffer
   if (ldy == 0) ldy = N;
@@ -661,7 +690,7 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
   int rc = current_device(&d);
   if (rc != DQ_OK) return rc;
   const Plan p = make_plan(fmt, M, N, K, d->sms, tp == nullptr, allow_twophase && tp == nullptr,
-                           tp == nullptr);
+                           tp == nullptr, max_split_ws);
   if (p.ws > 0 && (ws == nullptr || ws_bytes < p.ws || !aligned(ws, 16))) return DQ_ERR_WORKSPACE;
 
   if (p.smallm) {
@@ -1053,7 +1082,7 @@ int dq_linear_nf4_noalloc(const void* x, int64_t M, int64_t K, const uint8_t* pa
   DeviceInfo* d = nullptr;
   int rc = current_device(&d);
   if (rc != DQ_OK) return rc;
-  if (make_plan(kFmtNF4, M, N, K, d->sms, true, false).ws > DQ_NOALLOC_SCRATCH_BYTES)
+  if (make_plan(kFmtNF4, M, N, K, d->sms, true, false, true, DQ_NOALLOC_SCRATCH_BYTES).ws > DQ_NOALLOC_SCRATCH_BYTES)
     return DQ_ERR_SCRATCH_LIMIT;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return DQ_ERR_CUDA;
@@ -1070,7 +1099,8 @@ int dq_linear_nf4_noalloc(const void* x, int64_t M, int64_t K, const uint8_t* pa
     }
   }
   return linear_impl(kFmtNF4, x, M, K, packed, absmax, 0.f, bias, N, y, scratch,
-                     DQ_NOALLOC_SCRATCH_BYTES, static_cast<cudaStream_t>(stream), nullptr, false);
+                     DQ_NOALLOC_SCRATCH_BYTES, static_cast<cudaStream_t>(stream), nullptr, false,
+                     kActNone, 0, DQ_NOALLOC_SCRATCH_BYTES);
 }
 
 int dq_tp_buffer_alloc(size_t bytes, void** ptr) {

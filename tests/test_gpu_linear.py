@@ -321,6 +321,21 @@ def test_plan_choice(ops):
     assert ops.workspace_size(4, 3072, 3072) == 0
 
 
+@pytest.mark.parametrize("fmt", ["nf4", "fp8"])
+def test_long_k_split_plan(ops, fmt):
+    # long K on a partial wave: two K halves of one-CTA tiles fill the SMs once
+    f = 0 if fmt == "nf4" else 1
+    plan = ops.plan_info(512, 3072, 12288, f)
+    assert not plan["pair"] and not plan["twophase"] and plan["bm"] == 192 and plan["splits"] == 2
+    m, n, k = 300, 3072, 8192
+    plan = ops.plan_info(m, n, k, f)
+    assert not plan["pair"] and plan["splits"] == 2
+    x, w, bias, ref = _case(m, n, k, 5 + m, fmt, with_bias=True)
+    y = _run(ops, fmt, x, w, bias, n)
+    torch.cuda.synchronize()
+    assert R.rel_err(to_bits(y), ref) <= TOL
+
+
 def test_no_kernel_error_recorded(ops):
     assert ops.device_error() == 0
 
