@@ -9,6 +9,14 @@ per GPU) every rank runs its own token batch against a replicated weight: data
 parallel, no data-path collective, weak scaling; the value is the whole-job
 TFLOP/s from the max-over-ranks device time.
 
+The same run then measures, into the same JSON line, the rest of the
+benchmark suite at this N: the fp8 linear of the same shape (`fp8_linear`),
+the small-M sweep of the modulation projection (`small_m`), the four LTX
+video linears (`ltx_fp8`: single GPU at N = 1, column-parallel over the N
+GPUs with the fused NVLink all-gather at N > 1, with a bit-exactness check
+against the single-GPU kernel), and one FLUX.1 1024x1024 DiT step per GPU
+(`dit_step`: data parallel, one image per rank).
+
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload nf4|fp8]
     python bench.py --impl reference ...   # the reference's CPU algorithm
 """
@@ -60,6 +68,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile-kernels", action="store_true",
                     help="flux_dit: add the per-kernel device-time table of one eager step")
+    ap.add_argument("--extras", default="fp8,small,ltx,dit",
+                    help="default workload: comma list of the sections measured after the "
+                         "headline linear (fp8, small, ltx, dit) or 'none'")
     return ap.parse_args()
 
 
@@ -77,15 +88,21 @@ def measured_peaks():
 
 
 def profile_traffic(workload: str, plan: dict):
-    """DRAM bytes per launch of the planned kernel from its committed ncu summary."""
+    """(DRAM bytes per launch, source) of the planned kernel from its committed
+    ncu summary, only when that summary was captured on the same plan (its
+    `plan_bm:` line equals the x-tile height planned now); else (None, why).
+    The number is from an ncu capture, not measured in this run."""
     kern = "bf16_gemm2" if plan["twophase"] else ("dq_gemm2" if plan["pair"] else "dq_gemm")
-    path = os.path.join(ROOT, "profiles", f"{kern}_{workload}_4608x3072x12288.md")
+    name = f"{kern}_{workload}_4608x3072x12288.md"
     try:
-        txt = open(path).read()
+        txt = open(os.path.join(ROOT, "profiles", name)).read()
     except OSError:
-        return None
+        return None, f"no ncu summary of {kern} at this shape"
     m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", txt)
-    return float(m.group(1)) if m else None
+    b = re.search(r"plan_bm:\s*([0-9]+)", txt)
+    if not m or not b or int(b.group(1)) != plan["bm"]:
+        return None, f"profiles/{name} was captured on another plan"
+    return float(m.group(1)), f"ncu capture of the same plan (profiles/{name}), not this run"
 
 
 # ------------------------------------------------------------------ clocks
@@ -270,7 +287,19 @@ def cpu_reference_step_fn(workload: str, row_slice: int):
     return step, 2 * M * n_s * K, desc
 
 
+def host_threads() -> int:
+    """Use every host core this process may run on, whatever OMP_NUM_THREADS
+    the launcher set (torchrun sets 1)."""
+    try:
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:
+        n = os.cpu_count() or 1
+    torch.set_num_threads(max(1, n))
+    return torch.get_num_threads()
+
+
 def run_cpu_baseline(workload: str, budget_s: float = 12.0):
+    host_threads()
     step, flops, desc = cpu_reference_step_fn(workload, REF_ROW_SLICE)
     step()
     n = 0
@@ -285,9 +314,18 @@ def run_cpu_baseline(workload: str, budget_s: float = 12.0):
             "kind": "port", "sample": f"{desc}; {n} steps in {el:.1f} s"}
 
 
+def headline_config(fmt: str, world: int) -> dict:
+    """The headline workload's `config`, identical in both arms."""
+    return {"workload": WORKLOADS[fmt]["desc"], "format": fmt, "M": M, "N": N, "K": K,
+            "bias": False,
+            "parallelism": f"dp{world} (own token batch per GPU, replicated weight, no collective)",
+            "l2": f"{ROTATE} rotating input sets ({ROTATE * WORKLOADS[fmt]['bytes'] / 1e6:.0f} MB) > 126 MB L2"}
+
+
 def run_reference_arm(args, world, rank):
     if rank != 0:
         return
+    threads = host_threads()
     step, flops, desc = cpu_reference_step_fn(args.workload, REF_ROW_SLICE)
     for _ in range(args.warmup):
         step()
@@ -301,26 +339,66 @@ def run_reference_arm(args, world, rank):
         "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOADS[args.workload]["desc"], "format": args.workload,
-                   "parallelism": "host cores of rank 0"},
-        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+        "config": headline_config(args.workload, world),
+        "row_slice": REF_ROW_SLICE,
+        "reference_execution": (f"rank 0 only, {threads} host threads; each step runs the whole x "
+                                f"against 1/{REF_ROW_SLICE} of the weight rows and is counted by its "
+                                "own FLOPs"),
+        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": threads,
                          "kind": "port", "sample": desc},
         "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------ timing
+class Ctx:
+    """One rank's device, launch stream and place in the job."""
+
+    def __init__(self, args, world, rank, local):
+        self.args, self.world, self.rank, self.local = args, world, rank, local
+        torch.cuda.set_device(local)
+        self.dev = torch.device("cuda", local)
+        self.stream = torch.cuda.current_stream(self.dev)
+
+    def timed(self, fn, steps: int, warmup: int | None = None):
+        """Run fn(i) warmup times untimed, then `steps` times between CUDA
+        events on the launch stream, bracketed by a barrier and a synchronize
+        on both sides.  Returns (max over ranks of ms per step, per-rank ms)."""
+        for i in range(max(self.args.warmup if warmup is None else warmup, 3)):
+            fn(i)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(self.world)
+        torch.cuda.synchronize()
+        a.record(self.stream)
+        for i in range(steps):
+            fn(i)
+        b.record(self.stream)
+        torch.cuda.synchronize()
+        barrier(self.world)
+        ms = a.elapsed_time(b) / steps
+        return max_over_ranks(ms, self.world, self.dev), gather_ranks(ms, self.world, self.dev)
+
+
+def release(*_):
+    """Free what a section held before the next one starts."""
+    from diffuser_b200 import ops
+    ops.release_workspaces()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+
+
 # ------------------------------------------------------------------ our arm
 def run_ours(args, world, rank, local):
     from diffuser_b200 import _lib, modules, ops
 
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
+    ctx = Ctx(args, world, rank, local)
+    dev, stream = ctx.dev, ctx.stream
     if world > 1:
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     lib = _lib.lib()
-    stream = torch.cuda.current_stream(dev)
     sptr = ctypes.c_void_p(stream.cuda_stream)
     fmt = args.workload
 
@@ -458,37 +536,43 @@ def run_ours(args, world, rank, local):
                "api": "diffuser_b200.modules.ltx23_%s_linear.forward" % fmt,
                "copies": "pinned host buffers; upload, forward and download on three streams, "
                          "overlapped across consecutive steps"}
+        del mod, xh, yh, xd
 
     # ---- the reference's GPU algorithm on the same box, inputs and rotation:
     # decode the weight with its libtorch op sequence into the per-shape
-    # buffer, then torch.nn.functional.linear
-    ref_gpu = None
-    if world == 1:
-        rdq = RefGpuDequant(dev)
+    # buffer, then torch.nn.functional.linear (every rank, its own GPU)
+    rdq = RefGpuDequant(dev)
 
-        def ref_step(i):
-            x = xs[i % ROTATE]
-            wp, ap = wsets[i % ROTATE]
-            wb = rdq.nf4(wp, ap, N, K) if fmt == "nf4" else rdq.fp8(wp, scale)
-            return torch.nn.functional.linear(x, wb)
+    def ref_step(i):
+        x = xs[i % ROTATE]
+        wp, ap = wsets[i % ROTATE]
+        wb = rdq.nf4(wp, ap, N, K) if fmt == "nf4" else rdq.fp8(wp, scale)
+        return torch.nn.functional.linear(x, wb)
 
-        n_ref = max(10, min(args.steps, 100))
-        for i in range(3):
-            ref_step(i)
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        for i in range(n_ref):
-            ref_step(i)
-        b.record(stream)
-        torch.cuda.synchronize()
-        r_ms = a.elapsed_time(b) / n_ref
-        ref_gpu = {"value": FLOPS_PER_STEP / (r_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                   "ms_per_step": r_ms, "steps": n_ref,
-                   "algorithm": ("chunked byte-table gather + per-block mul into a bf16 buffer "
-                                 "(R/nf4_ltx23.R:77-115), then F.linear (cuBLAS)") if fmt == "nf4"
-                   else "copy_ upcast + mul_ by bf16 scale (R/fp8_ltx23.R:79-80), then F.linear (cuBLAS)"}
-        del rdq
+    r_ms, _ = ctx.timed(ref_step, max(10, min(args.steps, 100)))
+    ref_gpu = {"value": world * FLOPS_PER_STEP / (r_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "ms_per_step": r_ms, "steps": max(10, min(args.steps, 100)),
+               "algorithm": ("chunked byte-table gather + per-block mul into a bf16 buffer "
+                             "(R/nf4_ltx23.R:77-115), then F.linear (cuBLAS)") if fmt == "nf4"
+               else "copy_ upcast + mul_ by bf16 scale (R/fp8_ltx23.R:79-80), then F.linear (cuBLAS)"}
+    del rdq, xs, ys, wsets, ws
+    release()
+
+    # ---- the rest of the suite at this N, into the same line
+    extras = {}
+    wanted = [] if args.extras == "none" else [e.strip() for e in args.extras.split(",") if e.strip()]
+    if "fp8" in wanted and fmt == "nf4":
+        extras["fp8_linear"] = linear_section(ctx, "fp8")
+        release()
+    if "small" in wanted:
+        extras["small_m"] = {f: small_section(ctx, f)[0] for f in ("nf4", "fp8")}
+        release()
+    if "ltx" in wanted:
+        extras["ltx_fp8"] = ltx_section(ctx)
+        release()
+    if "dit" in wanted:
+        extras["dit_step"] = dit_section(ctx, reference=True)
+        release()
 
     if rank == 0:
         burst_tf, sustained_tf, peak_bw, peak_src = measured_peaks()
@@ -500,23 +584,22 @@ def run_ours(args, world, rank, local):
         peak_kind = "burst"
         achieved = FLOPS_PER_STEP / (kern_ms_max * 1e-3) / 1e12
         plan = ops.plan_info(M, N, K, 0 if fmt == "nf4" else 1)
-        traffic = profile_traffic(fmt, plan)
+        traffic, traffic_src = profile_traffic(fmt, plan)
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             cpu = run_cpu_baseline(fmt)
+        value = world * FLOPS_PER_STEP * args.steps / (el_ms_max * 1e-3) / 1e12
         line = {
             "metric": "NF4/fp8 quant-linear TFLOP/s",
-            "value": world * FLOPS_PER_STEP * args.steps / (el_ms_max * 1e-3) / 1e12,
+            "value": value,
             "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
             "ms_per_step": el_ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": WORKLOADS[fmt]["desc"], "format": fmt, "M": M, "N": N, "K": K,
-                       "bias": False, "parallelism": f"dp{world} (own token batch per GPU, replicated weight, no collective)",
-                       "l2": f"{ROTATE} rotating input sets ({ROTATE * WORKLOADS[fmt]['bytes'] / 1e6:.0f} MB) > 126 MB L2"},
+            "config": headline_config(fmt, world),
             # kernel_ms brackets one whole call: with the two-phase plan the
             # counter memset plus the GEMM launch that decodes its weight
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
-                         "frac": achieved / peak_tf, "traffic": traffic,
+                         "frac": achieved / peak_tf, "traffic": traffic, "traffic_source": traffic_src,
                          "peak_source": f"{peak_src} bf16 dense, {peak_kind}",
                          "frac_of_burst_peak": achieved / burst_tf,
                          "frac_of_sustained_peak": achieved / sustained_tf,
@@ -528,21 +611,136 @@ def run_ours(args, world, rank, local):
                          "algorithmic_bytes": WORKLOADS[fmt]["bytes"]},
             "cpu_baseline": cpu,
             "reference_gpu_algorithm": ref_gpu,
-            "speedup_vs_reference_gpu_algorithm": (
-                (world * FLOPS_PER_STEP * args.steps / (el_ms_max * 1e-3) / 1e12) / ref_gpu["value"]
-                if ref_gpu else None),
+            "speedup_vs_reference_gpu_algorithm": value / ref_gpu["value"],
             "e2e": e2e,
             "gpu_launches": args.steps * launches_per_step,
             "clocks": clocks,
         }
+        line.update(extras)
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
 
 
+# ------------------------------------------------------ fp8 linear (config 1)
+def linear_section(ctx, fmt: str) -> dict:
+    """The headline shape x[4608,3072] . W[12288,3072]^T in `fmt`, every rank
+    its own tokens, ROTATE input sets; device time per call, max over ranks."""
+    from diffuser_b200 import ops
+    dev = ctx.dev
+    w = torch.randn(N, K, generator=torch.Generator(device=dev).manual_seed(0), device=dev) * 0.02
+    if fmt == "nf4":
+        p0, a0 = ops.ltx23_nf4_quantize(w)
+        wsets = [(p0.clone(), a0.clone()) for _ in range(ROTATE)]
+        call = lambda i: ops.nf4_linear(xs[i % ROTATE], *wsets[i % ROTATE], N, out=ys[i % ROTATE])  # noqa: E731
+    else:
+        w80, s0 = ops.fp8_quantize(w)
+        scale = float(s0.item())
+        wsets = [w80.clone() for _ in range(ROTATE)]
+        call = lambda i: ops.fp8_linear(xs[i % ROTATE], wsets[i % ROTATE], scale, out=ys[i % ROTATE])  # noqa: E731
+    del w
+    xs = [torch.randn(M, K, generator=torch.Generator(device=dev).manual_seed(1 + 100 * ctx.rank + i),
+                      device=dev).to(torch.bfloat16) for i in range(ROTATE)]
+    ys = [torch.empty(M, N, dtype=torch.bfloat16, device=dev) for _ in range(ROTATE)]
+    ms, ranks = ctx.timed(call, ctx.args.steps)
+    plan = ops.plan_info(M, N, K, 0 if fmt == "nf4" else 1)
+    burst, sustained, _, src = measured_peaks()
+    tf = FLOPS_PER_STEP / (ms * 1e-3) / 1e12
+    return {"workload": WORKLOADS[fmt]["desc"], "ms_per_call": ms, "ms_per_call_per_rank": ranks,
+            "tflops_per_gpu": tf, "tflops_job": ctx.world * tf,
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": burst, "unit": "TFLOP/s",
+                         "frac": tf / burst, "peak_source": f"{src} bf16 dense, burst",
+                         "algorithmic_bytes": WORKLOADS[fmt]["bytes"]},
+            "mma": "tcgen05.mma kind::f16 (bf16 x bf16): the weight is decoded e4m3 -> bf16 "
+                   "bit-exactly as the reference's upcast x bf16(scale)" if fmt == "fp8" else
+                   "tcgen05.mma kind::f16 (bf16 x bf16) on the decoded NF4 weight",
+            "plan": plan, "l2": f"{ROTATE} rotating input sets > 126 MB L2"}
+
+
 # ------------------------------------------------------- column-parallel
 TP_M, TP_N, TP_K = 6144, 12288, 4096  # LTX video tokens x fused q/k/v projection (4096 -> 3 x 4096)
+LTX_M = 6144  # 121-frame 768x512 video: latent 16 x 16 x 24 tokens
+# (K, N, name): the LTX-2.3 transformer block's linears (R/dit_ltx23_modules.R:381-386,500-526)
+LTX_SHAPES = [(4096, 12288, "attn q/k/v (concatenated)"), (4096, 4096, "attn out"),
+              (4096, 16384, "ff up"), (16384, 4096, "ff down")]
+PEER_GBS = 770.0  # measured NVLink peer copy per direction per GPU on this B200 pool
+
+
+def ltx_section(ctx) -> dict:
+    """The four LTX video linears in fp8 at M = 6144 tokens.  One GPU: the
+    automatic single-GPU plan.  N > 1 GPUs: column-parallel over the ranks
+    (each computes [M, N/G] and its epilogue stores the block into every
+    rank's y over NVLink, then a bounded flag barrier), strong scaling; beside
+    it the NCCL all-gather path, and a bit-for-bit comparison of the assembled
+    y with the single-GPU kernel on the full weight."""
+    from diffuser_b200 import ops
+    dev, world = ctx.dev, ctx.world
+    burst, _, _, src = measured_peaks()
+    rows = []
+    grp = None
+    if world > 1:
+        from diffuser_b200 import tp
+        grp = tp.TpGroup(LTX_M, max(n for _, n, _ in LTX_SHAPES))
+    try:
+        for k, n, name in LTX_SHAPES:
+            w = torch.randn(n, k, generator=torch.Generator(device=dev).manual_seed(0), device=dev) * 0.02
+            w8, s0 = ops.fp8_quantize(w)  # the same weight on every rank
+            del w
+            scale = float(s0.item())
+            xs = [torch.randn(LTX_M, k, generator=torch.Generator(device=dev).manual_seed(1 + i),
+                              device=dev).to(torch.bfloat16) for i in range(2)]
+            flops = 2 * LTX_M * n * k
+            row = {"shape": f"x[{LTX_M},{k}] . W[{n},{k}]^T", "name": name, "K": k, "N": n,
+                   "compute_bound_ms": flops / world / (burst * 1e12) * 1e3}
+            if grp is None:
+                ys = [torch.empty(LTX_M, n, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+                ms, _ = ctx.timed(lambda i: ops.fp8_linear(xs[i % 2], w8, scale, out=ys[i % 2]),
+                                  ctx.args.steps)
+                row.update({"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12,
+                            "frac_of_burst_peak": flops / (ms * 1e-3) / 1e12 / burst,
+                            "kernel": ops.plan_info(LTX_M, n, k, 1)["kernel"]})
+                del ys
+            else:
+                from diffuser_b200 import tp
+                ref = ops.fp8_linear(xs[0], w8, scale)  # single-GPU kernel, full weight
+                mod = tp.ColumnParallelFp8Linear(k, n, grp, bias=False).to(dev)
+                mod.set_fp8_weight(w8, scale)
+                y = mod(xs[0])
+                torch.cuda.synchronize()
+                same = float(torch.equal(y, ref))
+                same_all = -max_over_ranks(-same, world, dev)  # min over ranks
+                del ref, y
+                fused, fused_ranks = ctx.timed(lambda i: mod(xs[i % 2]), ctx.args.steps)
+                nccl, _ = ctx.timed(lambda i: mod.forward_nccl(xs[i % 2]), ctx.args.steps)
+                peer = (world - 1) * LTX_M * (n // world) * 2  # bytes each rank sends
+                nvlink_bound = peer / (PEER_GBS * 1e9) * 1e3
+                row.update({"fused_ms": fused, "fused_ms_per_rank": fused_ranks,
+                            "nccl_allgather_path_ms": nccl,
+                            "tflops_job": flops / (fused * 1e-3) / 1e12,
+                            "tflops_per_gpu": flops / world / (fused * 1e-3) / 1e12,
+                            "nvlink_gbs_per_gpu": peer / (fused * 1e-3) / 1e9,
+                            "nvlink_bound_ms": nvlink_bound,
+                            "limiter": "nvlink" if nvlink_bound > row["compute_bound_ms"] else "compute",
+                            "frac_of_bound": max(nvlink_bound, row["compute_bound_ms"]) / fused,
+                            "parity_bitexact_vs_single_gpu": bool(same_all >= 1.0)})
+                del mod
+            rows.append(row)
+            del w8, xs
+            release()
+    finally:
+        if grp is not None:
+            grp.close()
+    out = {"workload": f"LTX-2.3 video DiT linears, fp8 e4m3 per-tensor, M={LTX_M} tokens",
+           "parallelism": f"tp{world} column-parallel over out_features, fused NVLink all-gather "
+                          "(epilogue peer stores + bounded flag barrier)" if world > 1 else "single GPU",
+           "scaling": "strong" if world > 1 else None,
+           "peak_source": f"{src} bf16 dense (burst); NVLink bound at the measured {PEER_GBS:.0f} GB/s "
+                          "peer copy per direction", "shapes": rows}
+    if world > 1:
+        out["parity_bitexact_all"] = all(r["parity_bitexact_vs_single_gpu"] for r in rows)
+        out["device_error"] = ops.device_error(dev)
+    return out
 
 
 def run_tp(args, world, rank, local):
@@ -552,8 +750,8 @@ def run_tp(args, world, rank, local):
     import torch.distributed as dist
     from diffuser_b200 import ops, tp
 
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
+    ctx = Ctx(args, world, rank, local)
+    dev = ctx.dev
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     else:
@@ -568,29 +766,14 @@ def run_tp(args, world, rank, local):
     del w8
     xs = [torch.randn(TP_M, TP_K, generator=torch.Generator(device=dev).manual_seed(1 + i),
                       device=dev).to(torch.bfloat16) for i in range(2)]
-    stream = torch.cuda.current_stream(dev)
-
-    def timed(fn, steps):
-        for i in range(max(args.warmup, 3)):
-            fn(i)
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier(world)
-        torch.cuda.synchronize()
-        a.record(stream)
-        for i in range(steps):
-            fn(i)
-        b.record(stream)
-        torch.cuda.synchronize()
-        barrier(world)
-        return max_over_ranks(a.elapsed_time(b) / steps, world, dev)
 
     with ClockSampler(local) as clk:
-        fused_ms = timed(lambda i: mod(xs[i % 2]), args.steps)
+        fused_ms, _ = ctx.timed(lambda i: mod(xs[i % 2]), args.steps)
     err = ops.device_error(dev)
     nccl_ms = None
     if world > 1:
-        nccl_ms = timed(lambda i: mod.forward_nccl(xs[i % 2]), max(10, args.steps // 4))
+        nccl_ms, _ = ctx.timed(lambda i: mod.forward_nccl(xs[i % 2]), max(10, args.steps // 4))
+    del mod
     grp.close()
     flops = 2 * TP_M * TP_N * TP_K
     peer_bytes = (world - 1) * TP_M * (TP_N // world) * 2  # sent by each rank
@@ -616,21 +799,24 @@ def run_tp(args, world, rank, local):
 
 
 # ------------------------------------------------------------ FLUX DiT step
-def run_flux(args, world, rank, local):
+DIT_CAST_FLOPS = 59.50e12  # the 494 cast linears of one step at 1024x1024, one image
+DIT_ATTN_FLOPS = 14.87e12  # 57 blocks x 4 x 4608^2 x 3072 (QK^T and PV)
+
+
+def dit_section(ctx, reference: bool = True, profile: bool = False) -> dict:
     """One flow-match Euler step of the FLUX.1 transformer at 1024x1024 (4096
     image + 512 text tokens) with its 494 cast linears in NF4 on the fused
-    engine, one image per GPU (latent seed 10 + rank).  Also times the same
-    step with the reference's linear algorithm (dequantize each NF4 weight
-    into a per-shape bf16 buffer, then cuBLAS) on the same model and box."""
-    import torch.distributed as dist
+    engine, one image per GPU (latent seed 10 + rank): data parallel, no
+    collective.  Timed eager and as a replayed CUDA graph; with `reference`
+    also the same step with the reference's linear algorithm (its libtorch NF4
+    decode ops into a per-shape bf16 buffer, then cuBLAS) and with the
+    engine's standalone dequantize kernel + cuBLAS."""
     from diffuser_b200 import flux, modules, ops
-
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    dev, world, args = ctx.dev, ctx.world, ctx.args
+    t0 = time.perf_counter()
     model = flux.build_flux_nf4(dev, seed=0)
-    g = torch.Generator().manual_seed(10 + rank)
+    build_s = time.perf_counter() - t0
+    g = torch.Generator().manual_seed(10 + ctx.rank)
     x = flux.pack_latents(torch.randn(1, 16, 128, 128, generator=g)).to(dev, torch.bfloat16)
     g1 = torch.Generator().manual_seed(3)
     text = torch.randn(1, 512, 4096, generator=g1).to(dev, torch.bfloat16)
@@ -638,30 +824,15 @@ def run_flux(args, world, rank, local):
     ids = torch.cat([torch.zeros(512, 3), flux.prepare_latent_image_ids(64, 64)], dim=0)
     rope = flux.pos_embed(ids.to(dev), (16, 56, 56))
     t = torch.ones(1, dtype=torch.float32, device=dev)
-    stream = torch.cuda.current_stream(dev)
 
-    def step():
+    def step(_i=0):
         with torch.no_grad():
             v = model(x, text, pooled, t, rope)
             return flux.euler_step(v, 1.0, 0.75, x)
 
-    def timed(steps):
-        for _ in range(max(args.warmup, 3)):
-            step()
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier(world)
-        torch.cuda.synchronize()
-        a.record(stream)
-        for _ in range(steps):
-            step()
-        b.record(stream)
-        torch.cuda.synchronize()
-        barrier(world)
-        return max_over_ranks(a.elapsed_time(b) / steps, world, dev)
-
-    with ClockSampler(local) as clk:
-        eager_ms = timed(args.steps)
+    steps = max(5, args.steps)
+    with ClockSampler(ctx.local) as clk:
+        eager_ms, eager_ranks = ctx.timed(step, steps)
         # the same step captured once in a CUDA graph and replayed (the engine
         # launches on torch's current stream with cached workspaces, so the
         # whole step captures)
@@ -669,27 +840,11 @@ def run_flux(args, world, rank, local):
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             step_out = step()
-        graph_steps = lambda: graph.replay()
-
-        def timed_graph(steps):
-            for _ in range(3):
-                graph_steps()
-            torch.cuda.synchronize()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            barrier(world)
-            torch.cuda.synchronize()
-            a.record(stream)
-            for _ in range(steps):
-                graph_steps()
-            b.record(stream)
-            torch.cuda.synchronize()
-            barrier(world)
-            return max_over_ranks(a.elapsed_time(b) / steps, world, dev)
-        ms = timed_graph(args.steps)
+        graph_ms, graph_ranks = ctx.timed(lambda i: graph.replay(), steps, warmup=3)
     err = ops.device_error(dev)
     del graph, step_out
     kernels = None
-    if args.profile_kernels:
+    if profile:
         # one eager step under the torch profiler (outside every timed region)
         torch.cuda.synchronize()
         with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
@@ -701,63 +856,88 @@ def run_flux(args, world, rank, local):
                    "top": [{"kernel": e.key[:120], "launches": e.count, "ms": e.device_time_total / 1e3,
                             "share": e.device_time_total / total}
                            for e in sorted(ka, key=lambda e: -e.device_time_total)[:16]]}
-    # The reference's algorithm for every NF4 linear, same weights: its
-    # libtorch decode ops into a per-shape bf16 buffer, then cuBLAS; and, for
-    # context, the engine's standalone dequantize kernel in place of those ops.
-    nf4 = [m for m in model.modules() if isinstance(m, modules.Ltx23Nf4Linear)]
-    rdq = RefGpuDequant(dev)
+    ref_ms = engine_dq_ms = None
+    if reference:
+        nf4 = [m for m in model.modules() if isinstance(m, modules.Ltx23Nf4Linear)]
+        rdq = RefGpuDequant(dev)
 
-    def swap_forward(decode):
-        saved = []
-        for m in nf4:
-            def fwd(xx, act=None, m=m):
-                w = decode(m)
-                y = torch.nn.functional.linear(xx, w, m.bias)
-                return torch.nn.functional.gelu(y, approximate="tanh") if act else y
-            saved.append((m, m.forward))
-            m.forward = fwd
-        return saved
+        def swap_forward(decode):
+            saved = []
+            for m in nf4:
+                def fwd(xx, act=None, m=m):
+                    w = decode(m)
+                    y = torch.nn.functional.linear(xx, w, m.bias)
+                    return torch.nn.functional.gelu(y, approximate="tanh") if act else y
+                saved.append((m, m.forward))
+                m.forward = fwd
+            return saved
 
-    # the reference calls q, k and v as three linears and concatenates with torch.cat
-    flux.FUSED_QKV = flux.FUSED_CONCAT = False
-    saved = swap_forward(lambda m: rdq.nf4(m.weight_nf4, m.weight_absmax, m.out_features,
-                                           m.in_features))
-    ref_ms = timed(max(3, args.steps // 2))
-    for m, f in saved:
-        m.forward = f
-    saved = swap_forward(lambda m: ops.ltx23_nf4_dequantize(
-        m.weight_nf4, m.weight_absmax, (m.out_features, m.in_features),
-        out=rdq.buffer(m.out_features, m.in_features)))
-    engine_dq_ms = timed(max(3, args.steps // 2))
-    for m, f in saved:
-        m.forward = f
-    flux.FUSED_QKV = flux.FUSED_CONCAT = True
-    del rdq
+        # the reference calls q, k and v as three linears and concatenates with torch.cat
+        flux.FUSED_QKV = flux.FUSED_CONCAT = False
+        try:
+            saved = swap_forward(lambda m: rdq.nf4(m.weight_nf4, m.weight_absmax, m.out_features,
+                                                   m.in_features))
+            ref_ms, _ = ctx.timed(step, max(3, steps // 2))
+            for m, f in saved:
+                m.forward = f
+            saved = swap_forward(lambda m: ops.ltx23_nf4_dequantize(
+                m.weight_nf4, m.weight_absmax, (m.out_features, m.in_features),
+                out=rdq.buffer(m.out_features, m.in_features)))
+            engine_dq_ms, _ = ctx.timed(step, max(3, steps // 2))
+            for m, f in saved:
+                m.forward = f
+        finally:
+            flux.FUSED_QKV = flux.FUSED_CONCAT = True
+        del rdq
+    del model
+    _, sustained, _, src = measured_peaks()
+    flops = DIT_CAST_FLOPS + DIT_ATTN_FLOPS
+    tf = flops / (graph_ms * 1e-3) / 1e12
+    spread = max(graph_ranks) / min(graph_ranks) - 1.0
+    out = {"workload": "FLUX.1-schnell transformer, 19 double + 38 single blocks, 4096 image + 512 "
+                       "text tokens (1024x1024), one flow-match Euler step, one image per GPU, NF4 "
+                       "cast linears (random N(0,0.02) weights)",
+           "parallelism": f"dp{world} (one image per rank, replicated weights, no collective)",
+           "graph_ms": graph_ms, "graph_ms_per_rank": graph_ranks,
+           "eager_ms": eager_ms, "eager_ms_per_rank": eager_ranks, "steps": steps,
+           "images_per_s_4_steps": world / (4 * graph_ms * 1e-3),
+           "reference_algorithm_step_ms": ref_ms,
+           "speedup_vs_reference_algorithm": (ref_ms / graph_ms) if ref_ms else None,
+           "engine_dequant_plus_cublas_step_ms": engine_dq_ms,
+           "flops_per_step": flops,
+           "roofline": {"bound": "tensor", "achieved": tf, "peak": sustained, "unit": "TFLOP/s",
+                        "frac": tf / sustained,
+                        "peak_source": f"{src} bf16 dense, sustained (the step runs back to back for seconds)"},
+           "limiter": (f"per-rank compute (no collective); slowest rank {spread * 100:.1f}% above the fastest"
+                       if world > 1 else "compute (tensor cores; kernel table in profiles/flux_dit_step_1024.md)"),
+           "model_build_s": build_s, "device_error": err, "clocks": clk.summary(),
+           "note": "graph_ms = the step replayed from a CUDA graph; eager_ms without; the reference "
+                   "algorithm step and the engine-dequantize + cuBLAS step are eager"}
+    if kernels is not None:
+        out["kernels_one_eager_step"] = kernels
+    return out
+
+
+def run_flux(args, world, rank, local):
+    """The DiT step alone, as its own line (value = graph step ms)."""
+    ctx = Ctx(args, world, rank, local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=ctx.dev)
+    d = dit_section(ctx, reference=True, profile=args.profile_kernels)
     if rank == 0:
-        cast_flops = 59.50e12  # cast linears per step at 1024x1024, B = 1
         line = {
-            "metric": "FLUX.1 1024x1024 DiT step ms", "value": ms, "unit": "ms", "n_gpus": world,
-            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
-            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "metric": "FLUX.1 1024x1024 DiT step ms", "value": d["graph_ms"], "unit": "ms",
+            "n_gpus": world, "steps": d["steps"], "warmup": max(args.warmup, 3),
+            "ms_per_step": d["graph_ms"], "higher_is_better": False, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random N(0,0.02) weights, NF4 cast linears)",
-            "config": {"workload": "FLUX.1 transformer, 19 double + 38 single blocks, 4096 image + 512 text "
-                                   "tokens, one Euler step, one image per GPU",
-                       "parallelism": f"dp{world} (replicas, no collective)"},
-            "eager_step_ms": eager_ms,
-            "images_per_s_4_steps": world / (4 * ms * 1e-3),
-            "cast_linear_tflops_if_all_time": cast_flops / (ms * 1e-3) / 1e12,
-            "reference_algorithm_step_ms": ref_ms,
-            "speedup_vs_reference_algorithm": ref_ms / ms,
-            "engine_dequant_plus_cublas_step_ms": engine_dq_ms,
-            "note": "value = the step replayed from a CUDA graph; eager_step_ms without; the reference "
-                    "algorithm step (its libtorch NF4 decode ops + cuBLAS per cast linear) and the "
-                    "engine-dequantize + cuBLAS step are eager",
-            "device_error": err, "clocks": clk.summary(),
+            "config": {"workload": d["workload"], "parallelism": d["parallelism"]},
+            "dit_step": d,
         }
-        if kernels is not None:
-            line["kernels_one_eager_step"] = kernels
         print(json.dumps(line), flush=True)
     if world > 1:
+        import torch.distributed as dist
         dist.destroy_process_group()
 
 
@@ -767,69 +947,87 @@ SMALL_MS = (1, 16, 64, 512)
 SMALL_ROTATE = 8  # 8 weight copies (255 MB NF4) > 126 MB L2
 
 
-def run_small(args, world, rank, local):
+def small_section(ctx, fmt: str, with_reference: bool = False) -> dict:
     """The small-M sweep: x[M, 3072] . W[18432, 3072]^T for M in 1, 16, 64,
     512, each as a CUDA graph of 40 calls over 8 rotating weight copies.
-    M <= 64 is HBM-bound on the weight, so the value is GB/s at M = 1 against
-    the measured HBM copy bandwidth; every M is reported."""
-    from diffuser_b200 import modules, ops
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    fmt = args.workload.split("_")[1]
+    M <= 64 is HBM-bound on the weight: GB/s against the measured HBM copy
+    bandwidth; M = 512 is compute-bound: TFLOP/s."""
+    from diffuser_b200 import ops
+    dev, args = ctx.dev, ctx.args
     n, k = SMALL_N, SMALL_K
-    stream = torch.cuda.current_stream(dev)
-    g0 = torch.Generator(device=dev).manual_seed(0)
-    w = torch.randn(n, k, generator=g0, device=dev) * 0.02
+    w = torch.randn(n, k, generator=torch.Generator(device=dev).manual_seed(0), device=dev) * 0.02
     if fmt == "nf4":
         p0, a0 = ops.ltx23_nf4_quantize(w)
         wsets = [(p0.clone(), a0.clone()) for _ in range(SMALL_ROTATE)]
         wbytes = n * k // 2 + n * k // 64 * 4
-        call = lambda i, x: ops.nf4_linear(x, *wsets[i % SMALL_ROTATE], n)
+        call = lambda i, x: ops.nf4_linear(x, *wsets[i % SMALL_ROTATE], n)  # noqa: E731
     else:
         w80, s0 = ops.fp8_quantize(w)
         scale = float(s0.item())
         wsets = [w80.clone() for _ in range(SMALL_ROTATE)]
         wbytes = n * k
-        call = lambda i, x: ops.fp8_linear(x, wsets[i % SMALL_ROTATE], scale)
+        call = lambda i, x: ops.fp8_linear(x, wsets[i % SMALL_ROTATE], scale)  # noqa: E731
     del w
     per_graph = 40
-    reps = max(1, args.steps // per_graph)
+    reps = max(1, args.steps // per_graph) if args.steps >= per_graph else 1
+    _, _, hbm, src = measured_peaks()
+    burst = measured_peaks()[0]
     rows = []
-    with ClockSampler(local) as clk:
-        for m in SMALL_MS:
-            gx = torch.Generator(device=dev).manual_seed(1 + 100 * rank)
-            x = torch.randn(m, k, generator=gx, device=dev).to(torch.bfloat16)
-            for i in range(max(args.warmup, 3)):
+    for m in SMALL_MS:
+        x = torch.randn(m, k, generator=torch.Generator(device=dev).manual_seed(1 + 100 * ctx.rank),
+                        device=dev).to(torch.bfloat16)
+        for i in range(max(args.warmup, 3)):
+            call(i, x)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(per_graph):
                 call(i, x)
-            torch.cuda.synchronize()
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                for i in range(per_graph):
-                    call(i, x)
-            graph.replay()
-            torch.cuda.synchronize()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            barrier(world)
-            torch.cuda.synchronize()
-            a.record(stream)
-            for _ in range(reps):
-                graph.replay()
-            b.record(stream)
-            torch.cuda.synchronize()
-            barrier(world)
-            us = max_over_ranks(a.elapsed_time(b) * 1e3 / (reps * per_graph), world, dev)
-            del graph
-            plan = ops.plan_info(m, n, k, 0 if fmt == "nf4" else 1)
-            byts = wbytes + m * k * 2 + m * n * 2
-            rows.append({"M": m, "us": us, "GB_per_s": byts / us / 1e3,
-                         "TFLOP_per_s": 2 * m * n * k / us / 1e6, "algorithmic_bytes": byts,
-                         "kernel": plan["kernel"], "tile_tokens": plan["bm"], "splits": plan["splits"]})
+        ms, _ = ctx.timed(lambda i: graph.replay(), reps, warmup=1)
+        us = ms * 1e3 / per_graph
+        del graph
+        plan = ops.plan_info(m, n, k, 0 if fmt == "nf4" else 1)
+        byts = wbytes + m * k * 2 + m * n * 2
+        gbs, tfs = byts / us / 1e3, 2 * m * n * k / us / 1e6
+        rows.append({"M": m, "us": us, "GB_per_s": gbs, "frac_of_hbm": gbs / hbm,
+                     "TFLOP_per_s": tfs, "frac_of_burst_bf16": tfs / burst,
+                     "bound": "hbm" if m <= 64 else "tensor", "algorithmic_bytes": byts,
+                     "kernel": plan["kernel"], "tile_tokens": plan["bm"], "splits": plan["splits"]})
     err = ops.device_error(dev)
     if err != 0:
         raise RuntimeError(f"kernel error word {err}")
+    out = {"workload": f"{fmt}_linear x[M,{k}]bf16 . W[{n},{k}]{fmt}^T (FLUX AdaLN modulation shape)",
+           "launch": f"CUDA graph of {per_graph} calls, {SMALL_ROTATE} rotating weight copies "
+                     f"({SMALL_ROTATE * wbytes / 1e6:.0f} MB) > 126 MB L2",
+           "peak_source": f"{src} HBM copy bandwidth {hbm:.0f} GB/s", "sweep": rows}
+    if with_reference:
+        # the reference's GPU algorithm at M = 1: decode the whole weight, then cuBLAS
+        rdq = RefGpuDequant(dev)
+        x1 = torch.randn(1, k, device=dev).to(torch.bfloat16)
+
+        def ref_step(i):
+            wb = rdq.nf4(*wsets[i % SMALL_ROTATE], n, k) if fmt == "nf4" else \
+                rdq.fp8(wsets[i % SMALL_ROTATE].view(torch.uint8), scale)
+            return torch.nn.functional.linear(x1, wb)
+        r_ms, _ = ctx.timed(ref_step, 20)
+        out["reference_gpu_algorithm_us_M1"] = r_ms * 1e3
+        del rdq
+    return out, wsets, (scale if fmt == "fp8" else None)
+
+
+def run_small(args, world, rank, local):
+    """The small-M sweep as its own line (value = GB/s at M = 1)."""
+    from diffuser_b200 import modules
+    ctx = Ctx(args, world, rank, local)
+    dev, stream = ctx.dev, ctx.stream
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    fmt = args.workload.split("_")[1]
+    n, k = SMALL_N, SMALL_K
+    with ClockSampler(local) as clk:
+        sec, wsets, scale = small_section(ctx, fmt, with_reference=(world == 1))
+    rows = sec["sweep"]
 
     # M = 1 end to end through the public module with host buffers: x up,
     # y down, every call
@@ -841,56 +1039,28 @@ def run_small(args, world, rank, local):
         mod.set_fp8_weight(wsets[0].view(torch.float8_e4m3fn), torch.tensor(scale))
     xh = torch.randn(1, k).to(torch.bfloat16).pin_memory()
     yh = torch.empty(1, n, dtype=torch.bfloat16).pin_memory()
-    n_e2e = max(10, min(args.steps, 200))
 
-    def e2e_step():
+    def e2e_step(_i):
         y = mod(xh.to(dev, non_blocking=True))
         yh.copy_(y, non_blocking=True)
 
-    for _ in range(3):
-        e2e_step()
-    torch.cuda.synchronize()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(stream)
-    for _ in range(n_e2e):
-        e2e_step()
-    b.record(stream)
-    torch.cuda.synchronize()
-    e_us = max_over_ranks(a.elapsed_time(b) * 1e3 / n_e2e, world, dev)
-
-    # the reference's GPU algorithm at M = 1: decode the whole weight, then cuBLAS
-    ref_us = None
-    if world == 1:
-        rdq = RefGpuDequant(dev)
-        x1 = torch.randn(1, k, device=dev).to(torch.bfloat16)
-
-        def ref_step(i):
-            wb = rdq.nf4(*wsets[i % SMALL_ROTATE], n, k) if fmt == "nf4" else rdq.fp8(wsets[i % SMALL_ROTATE].view(torch.uint8), scale)
-            return torch.nn.functional.linear(x1, wb)
-        for i in range(3):
-            ref_step(i)
-        torch.cuda.synchronize()
-        a.record(stream)
-        for i in range(20):
-            ref_step(i)
-        b.record(stream)
-        torch.cuda.synchronize()
-        ref_us = a.elapsed_time(b) * 1e3 / 20
-        del rdq
-
+    n_e2e = max(10, min(args.steps, 200))
+    e_ms, _ = ctx.timed(e2e_step, n_e2e)
+    e_us = e_ms * 1e3
+    del stream
+    ref_us = sec.get("reference_gpu_algorithm_us_M1")
     if rank == 0:
         _, _, hbm, peak_src = measured_peaks()
         r1 = rows[0]
         line = {
             "metric": f"{fmt.upper()} small-M quant-linear GB/s (M=1, {k}->{n})",
             "value": world * r1["GB_per_s"], "unit": "GB/s", "n_gpus": world,
-            "steps": reps * per_graph, "warmup": max(args.warmup, 3), "ms_per_step": r1["us"] / 1e3,
+            "steps": max(1, args.steps // 40) * 40, "warmup": max(args.warmup, 3), "ms_per_step": r1["us"] / 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
             "config": {"workload": f"{fmt}_linear x[M,{k}]bf16 . W[{n},{k}]{fmt}^T, M in {list(SMALL_MS)}",
                        "parallelism": f"dp{world} (replicas, no collective)",
-                       "l2": f"{SMALL_ROTATE} rotating weight copies ({SMALL_ROTATE * wbytes / 1e6:.0f} MB) > 126 MB L2",
-                       "launch": "CUDA graph of 40 calls"},
+                       "l2": sec["launch"], "launch": "CUDA graph of 40 calls"},
             "roofline": {"bound": "hbm", "achieved": r1["GB_per_s"], "peak": hbm, "unit": "GB/s",
                          "frac": r1["GB_per_s"] / hbm, "traffic": None,
                          "peak_source": f"{peak_src} HBM copy bandwidth",
@@ -902,7 +1072,7 @@ def run_small(args, world, rank, local):
             "e2e": {"value": world * r1["algorithmic_bytes"] / e_us / 1e3, "unit": "GB/s",
                     "h2d_bytes_per_step": k * 2, "d2h_bytes_per_step": n * 2, "us_per_step": e_us,
                     "api": f"diffuser_b200.modules.ltx23_{fmt}_linear.forward (eager, one call per step)"},
-            "gpu_launches": reps * per_graph,
+            "gpu_launches": max(1, args.steps // 40) * 40,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)

@@ -162,37 +162,51 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits,
 }
 
 // ------------------------------------------------------------ device cache
+// Per-device facts and one-time kernel set-up.  Host threads may call the
+// library concurrently: every flag below is set (release) only after the
+// values it guards are written under g_dev_mu, and is read (acquire) without
+// the lock, so a reader that sees a flag also sees those values.
 struct DeviceInfo {
-  int ok = 0;  // 1 = probed
+  std::atomic<int> ok;  // 1 = probed
   int major = 0, minor = 0, sms = 0;
-  int smem_set[2][2][6] = {};   // [column-parallel][fmt][bm]
-  int smem_set2[2][2][6] = {};
+  std::atomic<int> smem_set[2][2][6];   // [column-parallel][fmt][bm]
+  std::atomic<int> smem_set2[2][2][6];
   int max_pairs[2][6] = {};     // [fmt][bm]
-  int bf16_smem_set[3][6] = {};    // bf16 pair GEMM, [decoded format + 1][bm]
+  std::atomic<int> bf16_smem_set[3][6];    // bf16 pair GEMM, [decoded format + 1][bm]
   int bf16_max_pairs[3][6] = {};
-  int smallm_set[2][2][3] = {};    // small-M kernel, [fmt][token tiles - 1][row groups 1/2/4]
+  std::atomic<int> smallm_set[2][2][3];    // small-M kernel, [fmt][token tiles - 1][row groups 1/2/4]
 };
 
 constexpr int kMaxDevices = 64;
-static DeviceInfo g_dev[kMaxDevices];
+static DeviceInfo g_dev[kMaxDevices];  // static storage: every flag starts at zero
 static std::mutex g_dev_mu;
 static std::atomic<int> g_override_bm{0}, g_override_splits{0}, g_override_pair{0};
+
+// Runs init() once per flag (per device and kernel configuration), under the
+// device mutex; the flag is raised only when init succeeds.
+template <typename F>
+static int once_per_device(std::atomic<int>& flag, F&& init) {
+  if (flag.load(std::memory_order_acquire)) return DQ_OK;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (flag.load(std::memory_order_relaxed)) return DQ_OK;
+  const int rc = init();
+  if (rc == DQ_OK) flag.store(1, std::memory_order_release);
+  return rc;
+}
 
 static int current_device(DeviceInfo** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return DQ_ERR_CUDA;
   if (dev < 0 || dev >= kMaxDevices) return DQ_ERR_CUDA;
   DeviceInfo& d = g_dev[dev];
-  if (!d.ok) {
-    std::lock_guard<std::mutex> lk(g_dev_mu);
-    if (!d.ok) {
-      if (cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
-          cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
-          cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-        return DQ_ERR_CUDA;
-      d.ok = 1;
-    }
-  }
+  const int rc = once_per_device(d.ok, [&] {
+    if (cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return static_cast<int>(DQ_ERR_CUDA);
+    return static_cast<int>(DQ_OK);
+  });
+  if (rc != DQ_OK) return rc;
   *out = &d;
   if (d.major != 10) return DQ_ERR_ARCH;
   return DQ_OK;
@@ -289,8 +303,8 @@ static size_t twophase_counter_bytes(int n_tiles) {
 constexpr int kTwoPhaseGroupN = 16;
 
 // max_split_ws: the most split-K scratch the caller can hold (the
-// allocation-free entry point's built-in array); plans needing more split only
-// where they always did.
+// allocation-free entry point's built-in array): automatic plans split at most
+// as far as their partial sums fit it; only a forced split count can exceed it.
 static Plan make_plan(int fmt, int64_t M, int64_t N, int64_t K, int sms, bool allow_split = true,
                       bool allow_twophase = true, bool allow_smallm = true,
                       size_t max_split_ws = SIZE_MAX) {
@@ -405,6 +419,12 @@ static Plan make_plan(int fmt, int64_t M, int64_t N, int64_t K, int sms, bool al
     s = long_k_split;
   } else if (allow_split && !p.twophase && base_tiles * 2 <= units && KB >= 8) {
     s = std::min(std::min(units / base_tiles, KB / 4), 16);
+    // a caller with bounded scratch gets the most splits whose partial sums
+    // fit it (an unsplit plan needs none, so an automatic plan always fits)
+    if (max_split_ws != SIZE_MAX) {
+      const size_t per_split = static_cast<size_t>(M) * N * sizeof(float);
+      s = static_cast<int>(std::min<size_t>(s, std::max<size_t>(1, max_split_ws / per_split)));
+    }
   }
   s = (allow_split && !p.twophase) ? std::max(1, std::min(s, KB)) : 1;
   p.kb_per_split = (KB + s - 1) / s;
@@ -423,12 +443,13 @@ static int launch_gemm(DeviceInfo* d, const Plan& p, const CUtensorMap& mx, cons
   using C = GemmCfg<FMT, BM>;
   auto kern = dq_gemm_kernel<FMT, BM, TP>;
   const int bi = bm_index(BM);
-  if (!d->smem_set[TP][FMT][bi]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
-        cudaSuccess)
-      return DQ_ERR_LAUNCH;
-    d->smem_set[TP][FMT][bi] = 1;
-  }
+  const int rc = once_per_device(d->smem_set[TP][FMT][bi], [&] {
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) ==
+                   cudaSuccess
+               ? static_cast<int>(DQ_OK)
+               : static_cast<int>(DQ_ERR_LAUNCH);
+  });
+  if (rc != DQ_OK) return rc;
   kern<<<p.grid, C::kThreads, C::kSmemBytes, st>>>(mx, mw, a);
   return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
 }
@@ -441,17 +462,17 @@ static int pair_setup(DeviceInfo* d, cudaLaunchConfig_t& cfg) {
   using C = Gemm2Cfg<FMT, BM>;
   auto kern = dq_gemm2_kernel<FMT, BM, TP>;
   const int bi = bm_index(BM);
-  if (d->smem_set2[TP][FMT][bi]) return DQ_OK;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
-      cudaSuccess)
-    return DQ_ERR_LAUNCH;
-  int clusters = 0;
-  cfg.gridDim = dim3(2 * std::max(1, d->sms / 2));
-  if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1)
-    return DQ_ERR_LAUNCH;
-  d->max_pairs[FMT][bi] = clusters;
-  d->smem_set2[TP][FMT][bi] = 1;
-  return DQ_OK;
+  return once_per_device(d->smem_set2[TP][FMT][bi], [&] {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
+        cudaSuccess)
+      return static_cast<int>(DQ_ERR_LAUNCH);
+    int clusters = 0;
+    cfg.gridDim = dim3(2 * std::max(1, d->sms / 2));
+    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1)
+      return static_cast<int>(DQ_ERR_LAUNCH);
+    d->max_pairs[FMT][bi] = clusters;
+    return static_cast<int>(DQ_OK);
+  });
 }
 
 template <int FMT, int BM>
@@ -521,20 +542,20 @@ template <int BM, int FMT>
 static int bf16_pair_setup(DeviceInfo* d) {
   using C = Bf16PairCfg<BM, FMT>;
   const int bi = bm_index(BM);
-  if (d->bf16_smem_set[FMT + 1][bi]) return DQ_OK;
-  auto kern = bf16_gemm2_kernel<BM, FMT>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
-      cudaSuccess)
-    return DQ_ERR_LAUNCH;
-  cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = bf16_pair_config<BM, FMT>(attr, nullptr);
-  cfg.gridDim = dim3(2 * std::max(1, d->sms / 2));
-  int clusters = 0;
-  if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1)
-    return DQ_ERR_LAUNCH;
-  d->bf16_max_pairs[FMT + 1][bi] = clusters;
-  d->bf16_smem_set[FMT + 1][bi] = 1;
-  return DQ_OK;
+  return once_per_device(d->bf16_smem_set[FMT + 1][bi], [&] {
+    auto kern = bf16_gemm2_kernel<BM, FMT>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
+        cudaSuccess)
+      return static_cast<int>(DQ_ERR_LAUNCH);
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = bf16_pair_config<BM, FMT>(attr, nullptr);
+    cfg.gridDim = dim3(2 * std::max(1, d->sms / 2));
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1)
+      return static_cast<int>(DQ_ERR_LAUNCH);
+    d->bf16_max_pairs[FMT + 1][bi] = clusters;
+    return static_cast<int>(DQ_OK);
+  });
 }
 
 template <int FMT>
@@ -638,13 +659,13 @@ static int launch_smallm_cfg(DeviceInfo* d, const Plan& p, const void* x, const 
                              int64_t M, int64_t N, int64_t K, int act, int64_t ldy, cudaStream_t st) {
   using C = SmallMCfg<FMT, MT, R16>;
   auto kern = smallm_kernel<FMT, MT, R16>;
-  int& set = d->smallm_set[FMT][MT - 1][R16 == 4 ? 2 : R16 - 1];
-  if (!set) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
-        cudaSuccess)
-      return DQ_ERR_LAUNCH;
-    set = 1;
-  }
+  const int rc = once_per_device(d->smallm_set[FMT][MT - 1][R16 == 4 ? 2 : R16 - 1], [&] {
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) ==
+                   cudaSuccess
+               ? static_cast<int>(DQ_OK)
+               : static_cast<int>(DQ_ERR_LAUNCH);
+  });
+  if (rc != DQ_OK) return rc;
   kern<<<p.grid, C::kThreads, C::kSmemBytes, st>>>(
       static_cast<const __nv_bfloat16*>(x), w, absmax, scale,
       static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y),
@@ -691,6 +712,7 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
   if (rc != DQ_OK) return rc;
   const Plan p = make_plan(fmt, M, N, K, d->sms, tp == nullptr, allow_twophase && tp == nullptr,
                            tp == nullptr, max_split_ws);
+  if (max_split_ws != SIZE_MAX && p.ws > max_split_ws) return DQ_ERR_SCRATCH_LIMIT;
   if (p.ws > 0 && (ws == nullptr || ws_bytes < p.ws || !aligned(ws, 16))) return DQ_ERR_WORKSPACE;
 
   if (p.smallm) {
@@ -1077,13 +1099,12 @@ extern "C" {
 int dq_linear_nf4_noalloc(const void* x, int64_t M, int64_t K, const uint8_t* packed,
                           const float* absmax, const void* bias, int64_t N, void* y,
                           dq_stream_t stream) {
-  if (M < 0 || N <= 0 || K <= 0 || (K % 64) != 0) return DQ_ERR_SHAPE;
-  if (M == 0) return DQ_OK;
+  // Arguments are validated by linear_impl, in the same order as for
+  // dq_linear_nf4; a plan whose partial sums exceed the built-in array (only a
+  // forced split count) returns DQ_ERR_SCRATCH_LIMIT there, before any launch.
   DeviceInfo* d = nullptr;
   int rc = current_device(&d);
   if (rc != DQ_OK) return rc;
-  if (make_plan(kFmtNF4, M, N, K, d->sms, true, false, true, DQ_NOALLOC_SCRATCH_BYTES).ws > DQ_NOALLOC_SCRATCH_BYTES)
-    return DQ_ERR_SCRATCH_LIMIT;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return DQ_ERR_CUDA;
   void* scratch = g_noalloc_addr[dev].load();

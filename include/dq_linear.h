@@ -113,8 +113,11 @@ int dq_linear_fp8(const void* x, int64_t M, int64_t K,
  * reference.  Same math and arguments as dq_linear_nf4 minus the workspace:
  * split-K partial sums go to a scratch array built into the library
  * (DQ_NOALLOC_SCRATCH_BYTES = 8 MiB, held on every GPU that loads the
- * library until the process exits).  A shape whose split-K plan needs more
- * returns DQ_ERR_SCRATCH_LIMIT without launching anything.  The first call
+ * library until the process exits).  Large token counts run the fused
+ * kernels rather than the two-phase plan, and automatic plans split K only as
+ * far as their partial sums fit the array; a split count forced with
+ * dq_set_tile_override that needs more returns DQ_ERR_SCRATCH_LIMIT without
+ * launching anything (after the same argument checks as dq_linear_nf4).  The first call
  * on a device looks up the array's device address (make that first call
  * before any stream capture).  All calls share the one array: calls whose
  * kernels overlap on the GPU (different streams, no ordering) race on it.

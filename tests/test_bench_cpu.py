@@ -31,3 +31,31 @@ def test_reference_gpu_decode_restatement_matches_the_oracle():
 
 def test_nf4_levels_match_the_oracle_table():
     assert bench.NF4_LEVELS == T.NF4_TABLE
+
+
+def test_reference_arm_line_matches_the_gpu_arm_config_and_uses_every_core(capsys):
+    import json
+    import os
+    import types
+
+    torch.set_num_threads(1)  # what torchrun's OMP_NUM_THREADS=1 leaves behind
+    args = types.SimpleNamespace(workload="nf4", warmup=0, steps=1, gpus=2)
+    bench.run_reference_arm(args, world=2, rank=0)
+    line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert line["impl"] == "reference"
+    assert line["config"] == bench.headline_config("nf4", 2)
+    assert {"M", "N", "K", "format"} <= set(line["config"])
+    assert line["row_slice"] == bench.REF_ROW_SLICE
+    assert line["cpu_baseline"]["cores"] == len(os.sched_getaffinity(0))
+    assert line["e2e"]["h2d_bytes_per_step"] == 0
+    # the other ranks print nothing
+    bench.run_reference_arm(args, world=2, rank=1)
+    assert capsys.readouterr().out == ""
+
+
+def test_profile_traffic_is_keyed_to_the_plan():
+    plan = {"twophase": True, "pair": True, "bm": 256}
+    traffic, src = bench.profile_traffic("nf4", plan)
+    assert traffic is not None and traffic > 0 and "same plan" in src
+    traffic, src = bench.profile_traffic("nf4", dict(plan, bm=192))
+    assert traffic is None and "another plan" in src

@@ -1,7 +1,10 @@
 """The FLUX DiT port against the reference's own fixtures (CPU, float32):
 the tiny transformer's output, the rotary tables, the rotary application and
-the latent packing.  The fixtures live in the reference's test tree; these
-tests skip where it is not present."""
+the latent packing.  The fixtures are the reference's test vectors
+(inst/tinytest/fixtures/flux_model.safetensors and rope_flux.safetensors),
+committed as tests/golden/flux_reference_fixtures.safetensors by
+tests/golden/extract_flux_fixtures.py; DIFFUSER_REF_FIXTURES may name the
+reference's fixture directory to read the originals instead."""
 import os
 
 import pytest
@@ -9,15 +12,20 @@ import torch
 
 from diffuser_b200 import flux
 
-FIXTURES = os.environ.get("DIFFUSER_REF_FIXTURES", "/root/reference/inst/tinytest/fixtures")
+FIXTURES = os.environ.get("DIFFUSER_REF_FIXTURES")
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden",
+                      "flux_reference_fixtures.safetensors")
 
 
 def _load(name):
-    path = os.path.join(FIXTURES, name)
-    if not os.path.exists(path):
-        pytest.skip(f"reference fixture {name} not available")
     from safetensors.torch import load_file
-    return load_file(path)
+    if FIXTURES:
+        path = os.path.join(FIXTURES, name)
+        if not os.path.exists(path):
+            pytest.skip(f"reference fixture {name} not available")
+        return load_file(path)
+    stem = name[:-len(".safetensors")]
+    return {k[len(stem) + 1:]: v for k, v in load_file(GOLDEN).items() if k.startswith(stem + "/")}
 
 
 def _max_abs(a, b):
