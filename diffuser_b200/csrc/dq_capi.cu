@@ -20,6 +20,7 @@
 #include "dq_bf16gemm2.cuh"
 #include "dq_dit.cuh"
 #include "dq_smallm.cuh"
+#include "dq_smallm2.cuh"
 
 #define DQ_VERSION_STRING "dqlinear-b200 0.1.0 (sm_100a)"
 
@@ -175,6 +176,7 @@ struct DeviceInfo {
   std::atomic<int> bf16_smem_set[3][6];    // bf16 pair GEMM, [decoded format + 1][bm]
   int bf16_max_pairs[3][6] = {};
   std::atomic<int> smallm_set[2][2][3];    // small-M kernel, [fmt][token tiles - 1][row groups 1/2/4]
+  std::atomic<int> smallm2_set[2][2][3];   // small-M TMA-ring kernel, [fmt][CTAs per SM - 2][row groups]
 };
 
 constexpr int kMaxDevices = 64;
@@ -245,6 +247,9 @@ struct Plan {
   bool pair = false;      // CTA-pair tiles (256 weight rows per tile)
   bool twophase = false;  // dequantize into bf16 scratch, then the bf16 pair GEMM
   bool smallm = false;    // decode-sized M: register-decode warp MMAs (smallm_kernel)
+  bool ring = false;      // ... with the weight streamed through a TMA ring (smallm2_kernel)
+  int r16 = 1;            // small-M: 16-row groups per CTA
+  int cps = 2;            // small-M ring kernel: resident CTAs per SM
   int bm = 0, splits = 1, kb_per_split = 0;
   int m_tiles = 0, n_tiles = 0, tiles = 0, grid = 0;
   size_t ws = 0;
@@ -285,6 +290,40 @@ static int smallm_r16(int fmt, int64_t M, int64_t N, int sms) {
   if (fmt == kFmtNF4 && M <= 8 && 2 * ((N + 63) / 64) >= 3 * static_cast<int64_t>(sms)) return 4;
   return (N + 31) / 32 >= sms ? 2 : 1;
 }
+// Row groups per CTA (R16) and resident CTAs per SM (CPS) of the TMA-ring
+// small-M kernel: the configuration whose grid fills the largest share of the
+// resident slots in one wave (measured, M = 1, NF4: 3072 -> 12288 at R16 = 2
+// 15.3 us with two CTAs per SM, where the 384 CTAs need two waves, 10.6 us
+// with three; 3072 -> 18432 11.6 us at R16 = 4 / CPS = 2, 15.0 us with three
+// CTAs per SM, whose 288 CTAs then leave slots empty and have shallower rings).
+// Beyond one wave at three CTAs per SM: R16 = 4, CPS = 3.
+static void smallm2_config(int64_t N, int sms, int* r16_out, int* cps_out) {
+  double best = -1.0;
+  *r16_out = 4;
+  *cps_out = 3;
+  for (int cps : {3, 2})
+    for (int r16 : {4, 2, 1}) {
+      const int64_t grid = (N + 16 * r16 - 1) / (16 * r16);
+      const int64_t slots = static_cast<int64_t>(cps) * sms;
+      if (grid > slots) continue;
+      const double fill = static_cast<double>(grid) / static_cast<double>(slots);
+      if (fill > best + 1e-9) {
+        best = fill;
+        *r16_out = r16;
+        *cps_out = cps;
+      }
+    }
+}
+// The TMA-ring kernel serves one 8-token tile and takes NF4 block-scale tiles
+// by TMA (rows of K / 64 floats must be whole 16-byte units).  Automatic up to
+// four tokens: from about eight, every consumer lane reads x through an L1
+// that the ring's shared memory has mostly taken, and the register-stream
+// kernel is faster (3072 -> 18432 at M = 8: 16.9 against 13.6 us).
+constexpr int64_t kSmallM2AutoMaxM = 4;
+static bool smallm2_shape_ok(int fmt, int64_t M, int64_t K) {
+  return M <= 8 && (fmt == kFmtNF4 ? K % 256 == 0 : K % 128 == 0);
+}
+
 // Token count from which the two-phase plan is chosen: decoding the weight
 // once (~N*K*2.6 bytes of HBM traffic) costs less than decoding it in every
 // token tile, and the bf16 pair GEMM runs faster than the fused kernels.
@@ -317,14 +356,20 @@ static Plan make_plan(int fmt, int64_t M, int64_t N, int64_t K, int sms, bool al
   const int opair = g_override_pair.load();
   const int obm = g_override_bm.load();
   // Automatic for M <= 8 (one 8-token tile); for a second tile only with two
-  // row groups per CTA -- with one, the fused kernel is faster there.
+  // row groups per CTA -- with one, the fused kernel is faster there.  The
+  // TMA-ring kernel wherever its shape rule holds (pair mode 6 forces the
+  // register-stream kernel).
   if (allow_smallm && M <= kSmallMMaxM && K % 128 == 0 &&
-      (opair == 5 || (opair == 0 && obm == 0 && g_override_splits.load() == 0 &&
-                      (M <= 8 || smallm_r16(fmt, M, N, sms) >= 2)))) {
+      (opair == 5 || opair == 6 ||
+       (opair == 0 && obm == 0 && g_override_splits.load() == 0 &&
+        (M <= 8 || smallm_r16(fmt, M, N, sms) >= 2)))) {
     p.smallm = true;
+    p.ring = smallm2_shape_ok(fmt, M, K) && (opair == 5 || (opair == 0 && M <= kSmallM2AutoMaxM));
     p.bm = M <= 8 ? 8 : 16;
     p.m_tiles = 1;
-    const int r16 = smallm_r16(fmt, M, N, sms);
+    int r16 = smallm_r16(fmt, M, N, sms);
+    if (p.ring) smallm2_config(N, sms, &r16, &p.cps);
+    p.r16 = r16;
     p.n_tiles = static_cast<int>((N + 16 * r16 - 1) / (16 * r16));
     p.tiles = p.n_tiles;
     p.grid = p.n_tiles;
@@ -666,7 +711,8 @@ static int launch_smallm_cfg(DeviceInfo* d, const Plan& p, const void* x, const 
                : static_cast<int>(DQ_ERR_LAUNCH);
   });
   if (rc != DQ_OK) return rc;
-  kern<<<p.grid, C::kThreads, C::kSmemBytes, st>>>(
+  const int grid = static_cast<int>((N + 16 * R16 - 1) / (16 * R16));
+  kern<<<grid, C::kThreads, C::kSmemBytes, st>>>(
       static_cast<const __nv_bfloat16*>(x), w, absmax, scale,
       static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y),
       static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), act, ldy);
@@ -686,6 +732,70 @@ static int launch_smallm(DeviceInfo* d, const Plan& p, const void* x, const uint
       return launch_smallm_cfg<FMT, MT, 2>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
   }
   return launch_smallm_cfg<FMT, MT, 1>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
+}
+
+// The TMA-ring small-M kernel: one CTA per 16 * R16 weight rows, one 8-token
+// tile, CPS CTAs per SM.
+template <int FMT, int R16, int CPS>
+static int launch_smallm2_cfg(DeviceInfo* d, const void* x, const uint8_t* w, const float* absmax,
+                              float scale, const void* bias, void* y, int64_t M, int64_t N, int64_t K,
+                              int act, int64_t ldy, cudaStream_t st) {
+  using C = SmallM2Cfg<FMT, 1, R16, CPS>;
+  auto kern = smallm2_kernel<FMT, 1, R16, CPS>;
+  const int rc = once_per_device(d->smallm2_set[FMT][CPS - 2][R16 == 4 ? 2 : R16 - 1], [&] {
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) ==
+                   cudaSuccess
+               ? static_cast<int>(DQ_OK)
+               : static_cast<int>(DQ_ERR_LAUNCH);
+  });
+  if (rc != DQ_OK) return rc;
+  CUtensorMap mw, ma;
+  const uint64_t wrow = FMT == kFmtNF4 ? K / 2 : K;
+  if (!make_map_2d(&mw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, wrow, N, wrow, 128, C::kRows,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+    return DQ_ERR_CUDA;
+  if constexpr (FMT == kFmtNF4) {
+    if (!make_map_2d(&ma, absmax, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, K / 64, N, (K / 64) * 4,
+                     C::kAbsPerRow, C::kRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return DQ_ERR_CUDA;
+  } else {
+    ma = mw;  // unused
+  }
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>((N + C::kRows - 1) / C::kRows));
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, mw, ma, static_cast<const __nv_bfloat16*>(x), scale,
+                         static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y),
+                         static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), act,
+                         ldy) != cudaSuccess)
+    return DQ_ERR_LAUNCH;
+  return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
+}
+
+template <int FMT, int CPS>
+static int launch_smallm2_r(DeviceInfo* d, int r16, const void* x, const uint8_t* w, const float* absmax,
+                            float scale, const void* bias, void* y, int64_t M, int64_t N, int64_t K,
+                            int act, int64_t ldy, cudaStream_t st) {
+  switch (r16) {
+    case 4: return launch_smallm2_cfg<FMT, 4, CPS>(d, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
+    case 2: return launch_smallm2_cfg<FMT, 2, CPS>(d, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
+  }
+  return launch_smallm2_cfg<FMT, 1, CPS>(d, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
+}
+
+template <int FMT>
+static int launch_smallm2(DeviceInfo* d, const Plan& p, const void* x, const uint8_t* w,
+                          const float* absmax, float scale, const void* bias, void* y, int64_t M,
+                          int64_t N, int64_t K, int act, int64_t ldy, cudaStream_t st) {
+  return p.cps == 3 ? launch_smallm2_r<FMT, 3>(d, p.r16, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st)
+                    : launch_smallm2_r<FMT, 2>(d, p.r16, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
 }
 
 static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8_t* w,
@@ -715,6 +825,13 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
   if (max_split_ws != SIZE_MAX && p.ws > max_split_ws) return DQ_ERR_SCRATCH_LIMIT;
   if (p.ws > 0 && (ws == nullptr || ws_bytes < p.ws || !aligned(ws, 16))) return DQ_ERR_WORKSPACE;
 
+  if (p.smallm && p.ring && (fmt != kFmtNF4 || aligned(absmax, 16))) {
+    return fmt == kFmtNF4
+               ? launch_smallm2<kFmtNF4>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st)
+               : launch_smallm2<kFmtFP8>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
+  }
+  // (a ring plan whose NF4 scales are not 16-byte aligned falls through to the
+  // register-stream kernel, which picks its own row groups)
   if (p.smallm) {
     if (fmt == kFmtNF4)
       return p.bm <= 8 ? launch_smallm<kFmtNF4, 1>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st)
@@ -1048,7 +1165,7 @@ int dq_plan_info(int64_t M, int64_t N, int64_t K, int fmt, int* pair, int* bm, i
   const int rc = current_device(&d);
   if (rc != DQ_OK) return rc;
   const Plan p = make_plan(fmt, M, N, K, d->sms);
-  *pair = p.smallm ? 3 : p.twophase ? 2 : (p.pair ? 1 : 0);
+  *pair = p.smallm ? (p.ring ? 4 : 3) : p.twophase ? 2 : (p.pair ? 1 : 0);
   *bm = p.bm;
   *splits = p.splits;
   *grid = p.grid;
@@ -1308,7 +1425,7 @@ int dq_device_error(int* code, dq_stream_t stream) {
 }
 
 int dq_set_pair_mode(int mode) {
-  if (mode < 0 || mode > 5) return DQ_ERR_ARG;
+  if (mode < 0 || mode > 6) return DQ_ERR_ARG;
   g_override_pair.store(mode);
   return DQ_OK;
 }

@@ -274,7 +274,8 @@ def set_pair_mode(mode: int = 0) -> None:
     3 = two-phase (the bf16 pair GEMM launch dequantizes the weight into bf16
     scratch one group of weight tiles ahead of its MMAs), 4 = two-phase with
     the dequantization as a separate launch before the GEMM, 5 = the small-M
-    kernel (M <= 16, K % 128 == 0)."""
+    kernels (M <= 16, K % 128 == 0; the TMA-ring one where it applies),
+    6 = the small-M kernel that loads the weight into registers."""
     _lib.check("dq_set_pair_mode", _lib.lib().dq_set_pair_mode(int(mode)))
 
 
@@ -291,6 +292,9 @@ def plan_info(M: int, N: int, K: int, fmt: int = _lib.DQ_FMT_NF4) -> dict:
     pair, bm, splits, grid = (v.value for v in vals)
     kernel = {0: "dq_gemm_kernel (one CTA)", 1: "dq_gemm2_kernel (CTA pair)",
               2: "bf16_gemm2_kernel (CTA pair, decoding its weight in-launch)",
-              3: "smallm_kernel (weights decoded into warp-MMA registers)"}[pair]
-    return {"kernel": kernel, "pair": pair in (1, 2), "twophase": pair == 2, "smallm": pair == 3,
+              3: "smallm_kernel (weights loaded into registers, decoded into warp-MMA operands)",
+              4: "smallm2_kernel (weights streamed through a TMA ring, decoded into warp-MMA "
+                 "operands)"}[pair]
+    return {"kernel": kernel, "pair": pair in (1, 2), "twophase": pair == 2, "smallm": pair in (3, 4),
+            "ring": pair == 4,
             "bm": bm, "splits": splits, "grid": grid}

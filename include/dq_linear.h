@@ -142,8 +142,12 @@ int dq_set_tile_override(int bm, int splits);
  * (part of the workspace) by the bf16 CTA-pair GEMM launch itself, one group
  * of weight tiles ahead of its MMAs (automatic for M >= 1024), 4 = two-phase
  * with the dequantization as a separate launch before the GEMM, 5 = the
- * small-M kernel (weights decoded into warp-MMA registers; M <= 16 and
- * K % 128 == 0, automatic for M <= 8 and for M <= 16 when N >= 32 * SMs). */
+ * small-M kernels (weights decoded into warp-MMA registers; M <= 16 and
+ * K % 128 == 0, automatic for M <= 8 and for M <= 16 when N >= 32 * SMs):
+ * for M <= 8 the weight streamed through a TMA ring in shared memory where
+ * K % 256 == 0 (NF4) / K % 128 == 0 (fp8) and the NF4 absmax is 16-byte
+ * aligned (automatic for M <= 4), else loaded straight into registers; 6 =
+ * the small-M kernel that loads the weight straight into registers, always. */
 int dq_set_pair_mode(int mode);
 
 /* ------------------------------------------------- column-parallel linear
@@ -211,9 +215,11 @@ int dq_linear_fp8_ld(const void* x, int64_t M, int64_t K, const uint8_t* w8, flo
 /* Describes the launch plan dq_linear_* uses for this shape on the current
  * device: *pair = 0 for fused one-CTA tiles (128 weight rows), 1 for fused
  * CTA-pair tiles (256 rows), 2 for the two-phase plan (the bf16 CTA-pair GEMM
- * whose launch also dequantizes the weight into scratch), 3 for the small-M kernel (*bm = 8 or 16 tokens, 16, 32 or
- * 64 weight rows per CTA); *bm = x-tile rows, *splits = split-K count, *grid = CTAs
- * launched.  A diagnostic query with no reference counterpart. */
+ * whose launch also dequantizes the weight into scratch), 3 for the small-M kernel
+ * that loads the weight into registers, 4 for the small-M kernel that streams
+ * it through a TMA ring (*bm = 8 or 16 tokens; 16, 32 or 64 weight rows per
+ * CTA); *bm = x-tile rows, *splits = split-K count, *grid = CTAs launched.  A
+ * diagnostic query with no reference counterpart. */
 int dq_plan_info(int64_t M, int64_t N, int64_t K, int fmt, int* pair, int* bm, int* splits,
                  int* grid);
 

@@ -162,15 +162,18 @@ def test_split_k(ops, fmt, m, n, k, splits):
                                              (16, 1000, 1152, False), (16, 18432, 3072, True),
                                              (2, 3072, 15360, True), (5, 9000, 256, True),
                                              (1, 18432, 512, False)])
-def test_small_m_kernel(ops, fmt, m, n, k, with_bias):
+@pytest.mark.parametrize("mode", [5, 6])
+def test_small_m_kernel(ops, fmt, m, n, k, with_bias, mode):
     # decode-sized token counts: weights decoded straight into warp-MMA
     # registers (one and two 8-token tiles; one, two and four 16-row groups
-    # per CTA; ragged N; long K)
+    # per CTA; ragged N; long K), the weight streamed through the TMA ring
+    # (mode 5, where K allows) or loaded into registers (mode 6)
     x, w, bias, ref = _case(m, n, k, 23 + m + n, fmt, with_bias=with_bias)
-    ops.set_pair_mode(5)
+    ops.set_pair_mode(mode)
     try:
         plan = ops.plan_info(m, n, k, 0 if fmt == "nf4" else 1)
         assert plan["smallm"] and plan["splits"] == 1
+        assert plan["ring"] == (mode == 5 and m <= 8 and k % (256 if fmt == "nf4" else 128) == 0)
         y = _run(ops, fmt, x, w, bias, n)
         y2 = _run(ops, fmt, x, w, bias, n)
         torch.cuda.synchronize()
@@ -178,6 +181,47 @@ def test_small_m_kernel(ops, fmt, m, n, k, with_bias):
         ops.set_pair_mode(0)
     assert R.rel_err(to_bits(y), ref) <= TOL
     assert torch.equal(y, y2)
+    assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("fmt", ["nf4", "fp8"])
+@pytest.mark.parametrize("m,n,k", [(1, 18432, 3072), (8, 3072, 3072), (4, 9216, 3072),
+                                   (1, 12288, 4096), (3, 1000, 15360), (2, 200, 256)])
+def test_small_m_ring_and_register_kernels_agree(ops, fmt, m, n, k):
+    # the two small-M kernels decode the same weights into the same MMA
+    # fragments in the same k order; the ring kernel alternates two
+    # accumulators, so the sums differ only by f32 rounding
+    x, w, bias, ref = _case(m, n, k, 5 + m + n, fmt, with_bias=True)
+    outs = {}
+    for mode in (5, 6):
+        ops.set_pair_mode(mode)
+        try:
+            outs[mode] = _run(ops, fmt, x, w, bias, n)
+            torch.cuda.synchronize()
+        finally:
+            ops.set_pair_mode(0)
+        assert R.rel_err(to_bits(outs[mode]), ref) <= TOL, mode
+    assert R.rel_err(to_bits(outs[5]), to_bits(outs[6])) <= TOL
+
+
+def test_small_m_ring_falls_back_on_unaligned_scales(ops):
+    # the ring kernel copies NF4 block scales by TMA (16-byte aligned rows);
+    # a 4-byte aligned absmax view takes the register-stream kernel instead
+    m, n, k = 4, 4096, 3072
+    x, (p, a), bias, ref = _case(m, n, k, 77, "nf4", with_bias=True)
+    buf = torch.empty(a.numel() + 1, dtype=torch.float32, device="cuda")
+    buf[1:].copy_(a)
+    shifted = buf[1:]
+    assert shifted.data_ptr() % 16 != 0
+    ops.set_pair_mode(5)
+    try:
+        assert ops.plan_info(m, n, k, 0)["ring"]
+        y = ops.nf4_linear(x.cuda(), p, shifted, n, bias.cuda())
+        torch.cuda.synchronize()
+    finally:
+        ops.set_pair_mode(0)
+    assert R.rel_err(to_bits(y), ref) <= TOL
+    assert ops.device_error() == 0
 
 
 def test_leading_dims_and_noncontiguous_input(ops):
@@ -271,7 +315,8 @@ def test_golden_linear(ops):
                                                   (3, 256, 0, 300, 640, 512),   # two-phase
                                                   (4, 256, 0, 300, 640, 512),   # two launches
                                                   (1, 0, 3, 16, 640, 1088),     # split-K reduce
-                                                  (5, 0, 0, 12, 640, 1024)])    # small-M kernel
+                                                  (5, 0, 0, 12, 640, 1024),     # small-M, TMA ring
+                                                  (6, 0, 0, 12, 640, 1024)])    # small-M, registers
 def test_gelu_tanh_epilogue(ops, fmt, mode, bm, splits, m, n, k):
     # y = bf16(gelu_tanh(bf16(x W^T + b))) in the epilogue equals the linear
     # followed by torch's GELU-tanh on its bf16 output (the reference's
@@ -312,8 +357,11 @@ def test_plan_choice(ops):
     assert not mid["twophase"]
     # decode-sized batches: the small-M kernel (one 8-token tile always, two
     # only with two 16-row groups per CTA), else fused one-CTA tiles
-    assert ops.plan_info(1, 18432, 3072)["smallm"]
+    assert ops.plan_info(1, 18432, 3072)["smallm"] and ops.plan_info(1, 18432, 3072)["ring"]
     assert ops.plan_info(8, 3072, 3072)["bm"] == 8
+    assert not ops.plan_info(4, 3072, 3200)["ring"]  # NF4 K % 256 != 0: register-stream kernel
+    assert ops.plan_info(4, 3072, 3200, 1)["ring"]
+    assert not ops.plan_info(8, 18432, 3072)["ring"]  # from 5 tokens: register-stream kernel
     assert ops.plan_info(16, 18432, 3072)["smallm"]
     small = ops.plan_info(16, 3072, 3072)
     assert not small["smallm"] and not small["pair"] and small["bm"] == 16 and small["splits"] > 1
@@ -341,7 +389,8 @@ def test_no_kernel_error_recorded(ops):
 
 
 @pytest.mark.parametrize("fmt", ["nf4", "fp8"])
-@pytest.mark.parametrize("mode,splits,m", [(0, 0, 4),      # small-M kernel
+@pytest.mark.parametrize("mode,splits,m", [(0, 0, 4),      # small-M kernel (TMA ring)
+                                           (6, 0, 4),      # small-M kernel (registers)
                                            (1, 0, 300),    # fused one-CTA tiles
                                            (2, 0, 300),    # fused CTA pairs
                                            (1, 3, 16),     # split-K + reduce
