@@ -67,7 +67,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile-kernels", action="store_true",
-                    help="flux_dit: add the per-kernel device-time table of one eager step")
+                    help="flux_dit: add the per-kernel device-time table of three graph replays")
     ap.add_argument("--extras", default="fp8,small,ltx,dit",
                     help="default workload: comma list of the sections measured after the "
                          "headline linear (fp8, small, ltx, dit) or 'none'")
@@ -841,21 +841,36 @@ def dit_section(ctx, reference: bool = True, profile: bool = False) -> dict:
         with torch.cuda.graph(graph):
             step_out = step()
         graph_ms, graph_ranks = ctx.timed(lambda i: graph.replay(), steps, warmup=3)
-    err = ops.device_error(dev)
-    del graph, step_out
     kernels = None
     if profile:
-        # one eager step under the torch profiler (outside every timed region)
+        # Three graph replays back to back under the torch profiler (outside
+        # every timed region), bracketed by CUDA events and with the SM clock
+        # sampled: the kernels' summed device time per replay against the
+        # replay's own event time, at the same clocks, shows how much of the
+        # step is gaps between kernels rather than kernel time.
         torch.cuda.synchronize()
-        with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
-            step()
-            torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(ctx.local) as pclk:
+            with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+                a.record(ctx.stream)
+                for _ in range(3):
+                    graph.replay()
+                b.record(ctx.stream)
+                torch.cuda.synchronize()
+        replay_ms = a.elapsed_time(b) / 3
         ka = prof.key_averages()
-        total = sum(e.device_time_total for e in ka)
-        kernels = {"total_ms": total / 1e3,
-                   "top": [{"kernel": e.key[:120], "launches": e.count, "ms": e.device_time_total / 1e3,
-                            "share": e.device_time_total / total}
-                           for e in sorted(ka, key=lambda e: -e.device_time_total)[:16]]}
+        total = sum(e.device_time_total for e in ka) / 3
+        launches = sum(e.count for e in ka) / 3
+        kernels = {"replays": 3, "replay_ms_event": replay_ms, "kernel_ms_sum_per_replay": total / 1e3,
+                   "kernels_per_replay": launches,
+                   "gap_ms_per_replay": replay_ms - total / 1e3,
+                   "clocks": pclk.summary(),
+                   "top": [{"kernel": e.key[:120], "launches_per_replay": e.count / 3,
+                            "ms_per_replay": e.device_time_total / 3e3,
+                            "share": e.device_time_total / 3 / total}
+                           for e in sorted(ka, key=lambda e: -e.device_time_total)[:24]]}
+    err = ops.device_error(dev)
+    del graph, step_out
     ref_ms = engine_dq_ms = None
     if reference:
         nf4 = [m for m in model.modules() if isinstance(m, modules.Ltx23Nf4Linear)]
@@ -914,7 +929,7 @@ def dit_section(ctx, reference: bool = True, profile: bool = False) -> dict:
            "note": "graph_ms = the step replayed from a CUDA graph; eager_ms without; the reference "
                    "algorithm step and the engine-dequantize + cuBLAS step are eager"}
     if kernels is not None:
-        out["kernels_one_eager_step"] = kernels
+        out["kernels_graph_replay"] = kernels
     return out
 
 
