@@ -82,7 +82,7 @@ DQ_ERR_TIMEOUT = 5
 DQ_ERR_SCRATCH_LIMIT = 9
 DQ_NOALLOC_SCRATCH_BYTES = 8 << 20
 DQ_IPC_HANDLE_BYTES = 64
-DQ_ACT_NONE, DQ_ACT_GELU_TANH = 0, 1
+DQ_ACT_NONE, DQ_ACT_GELU_TANH, DQ_ACT_SWIGLU, DQ_ACT_GEGLU_TANH = 0, 1, 2, 3
 DQ_FMT_NF4, DQ_FMT_FP8 = 0, 1
 DQ_DTYPE_F32, DQ_DTYPE_BF16 = 0, 1
 

@@ -292,38 +292,44 @@ __global__ void __launch_bounds__(Bf16PairCfg<BM, FMT>::kThreads, 1)
         const int mrow0 = m0 + EC * (c0 + c);
         // stage [EC tokens][32 outputs] bf16, then write 64-byte row segments
         __nv_bfloat16* sb = reinterpret_cast<__nv_bfloat16*>(stg);
-        if (args.act == kActNone) {
-#pragma unroll
-          for (int j = 0; j < EC; ++j)
-            sts16(stg_s + 2u * (j * 32 + lane),
-                  __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(vc[j]) + bias)));
+        if (act_is_gated(args.act)) {
+          gated_chunk_store<EC>(vc, bias, args.act, stg_s, sb,
+                                reinterpret_cast<__nv_bfloat16*>(args.outs[0]), args.ldy, args.M,
+                                args.N / 2, mrow0, ncol0 / 2, args.vec_ok, lane);
         } else {
+          if (args.act == kActNone) {
 #pragma unroll
-          for (int j = 0; j < EC; ++j)
-            sts16(stg_s + 2u * (j * 32 + lane),
-                  __bfloat16_as_ushort(__float2bfloat16_rn(
-                      apply_act(__uint_as_float(vc[j]) + bias, args.act))));
-        }
-        __syncwarp();
-        __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(args.outs[0]);
+            for (int j = 0; j < EC; ++j)
+              sts16(stg_s + 2u * (j * 32 + lane),
+                    __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(vc[j]) + bias)));
+          } else {
 #pragma unroll
-        for (int i = 0; i < EC / 8; ++i) {
-          const int row = (lane >> 2) + 8 * i;
-          const int col = (lane & 3) * 8;
-          const int m = mrow0 + row;
-          const int nc = ncol0 + col;
-          if (m < args.M) {
-            __nv_bfloat16* dst = y + static_cast<size_t>(m) * args.ldy + nc;
-            if (args.vec_ok && nc + 8 <= args.N) {
-              *reinterpret_cast<uint4*>(dst) = lds128(stg_s + 2u * (row * 32 + col));
-            } else {
-              const __nv_bfloat16* src = sb + row * 32 + col;
-              for (int e = 0; e < 8; ++e)
-                if (nc + e < args.N) dst[e] = src[e];
+            for (int j = 0; j < EC; ++j)
+              sts16(stg_s + 2u * (j * 32 + lane),
+                    __bfloat16_as_ushort(__float2bfloat16_rn(
+                        apply_act(__uint_as_float(vc[j]) + bias, args.act))));
+          }
+          __syncwarp();
+          __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(args.outs[0]);
+#pragma unroll
+          for (int i = 0; i < EC / 8; ++i) {
+            const int row = (lane >> 2) + 8 * i;
+            const int col = (lane & 3) * 8;
+            const int m = mrow0 + row;
+            const int nc = ncol0 + col;
+            if (m < args.M) {
+              __nv_bfloat16* dst = y + static_cast<size_t>(m) * args.ldy + nc;
+              if (args.vec_ok && nc + 8 <= args.N) {
+                *reinterpret_cast<uint4*>(dst) = lds128(stg_s + 2u * (row * 32 + col));
+              } else {
+                const __nv_bfloat16* src = sb + row * 32 + col;
+                for (int e = 0; e < 8; ++e)
+                  if (nc + e < args.N) dst[e] = src[e];
+              }
             }
           }
+          __syncwarp();
         }
-        __syncwarp();
       }
       if (++acc == C::kNumAcc) { acc = 0; accphase ^= 1u; }
     }

@@ -147,12 +147,34 @@ __global__ void tp_wait_kernel(const unsigned int* flags, int world, unsigned in
   }
 }
 
-// Split-K: y[m, n] (row stride ldy) = bf16(sum_s partial[s][m, n] + bias).
+// Split-K: y[m, n] (row stride ldy) = bf16(sum_s partial[s][m, n] + bias);
+// with a gated activation y[m, j] (j < N / 2) from the gate row
+// 32 * (j / 16) + j % 16 and the up row 16 further (the gated row order).
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int M, int N,
                                      const __nv_bfloat16* __restrict__ bias,
                                      __nv_bfloat16* __restrict__ y, int act, int64_t ldy) {
   const int64_t total = static_cast<int64_t>(M) * N;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  if (act_is_gated(act)) {
+    const int no = N / 2;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+         i < static_cast<int64_t>(M) * no; i += stride) {
+      const int64_t m = i / no;
+      const int j = static_cast<int>(i - m * no);
+      const int ng = 32 * (j / 16) + j % 16;
+      float g = 0.f, u = 0.f;
+      for (int s = 0; s < splits; ++s) {
+        g += part[static_cast<size_t>(s) * total + m * N + ng];
+        u += part[static_cast<size_t>(s) * total + m * N + ng + 16];
+      }
+      if (bias != nullptr) {
+        g += __bfloat162float(bias[ng]);
+        u += __bfloat162float(bias[ng + 16]);
+      }
+      y[m * ldy + j] = __float2bfloat16_rn(gated_value(g, u, act));
+    }
+    return;
+  }
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total; i += stride) {
     float acc = 0.f;
     for (int s = 0; s < splits; ++s) acc += part[static_cast<size_t>(s) * total + i];
@@ -297,12 +319,13 @@ static int smallm_r16(int fmt, int64_t M, int64_t N, int sms) {
 // with three; 3072 -> 18432 11.6 us at R16 = 4 / CPS = 2, 15.0 us with three
 // CTAs per SM, whose 288 CTAs then leave slots empty and have shallower rings).
 // Beyond one wave at three CTAs per SM: R16 = 4, CPS = 3.
-static void smallm2_config(int64_t N, int sms, int* r16_out, int* cps_out) {
+static void smallm2_config(int64_t N, int sms, bool gated, int* r16_out, int* cps_out) {
   double best = -1.0;
   *r16_out = 4;
   *cps_out = 3;
   for (int cps : {3, 2})
     for (int r16 : {4, 2, 1}) {
+      if (gated && r16 == 1) continue;  // a gate / up pair of row groups per CTA
       const int64_t grid = (N + 16 * r16 - 1) / (16 * r16);
       const int64_t slots = static_cast<int64_t>(cps) * sms;
       if (grid > slots) continue;
@@ -322,6 +345,13 @@ static void smallm2_config(int64_t N, int sms, int* r16_out, int* cps_out) {
 constexpr int64_t kSmallM2AutoMaxM = 4;
 static bool smallm2_shape_ok(int fmt, int64_t M, int64_t K) {
   return M <= 8 && (fmt == kFmtNF4 ? K % 256 == 0 : K % 128 == 0);
+}
+
+// Row groups per CTA of the register-stream small-M kernel; a gated
+// activation needs its gate and up row groups in one CTA (an even count).
+static int smallm_rows(int fmt, int64_t M, int64_t N, int sms, bool gated) {
+  const int r16 = smallm_r16(fmt, M, N, sms);
+  return gated ? std::max(r16, 2) : r16;
 }
 
 // Token count from which the two-phase plan is chosen: decoding the weight
@@ -346,7 +376,7 @@ constexpr int kTwoPhaseGroupN = 16;
 // as far as their partial sums fit it; only a forced split count can exceed it.
 static Plan make_plan(int fmt, int64_t M, int64_t N, int64_t K, int sms, bool allow_split = true,
                       bool allow_twophase = true, bool allow_smallm = true,
-                      size_t max_split_ws = SIZE_MAX) {
+                      size_t max_split_ws = SIZE_MAX, bool gated = false) {
   Plan p;
   int long_k_split = 0;
   const int KB = static_cast<int>((K + 63) / 64);
@@ -367,8 +397,8 @@ static Plan make_plan(int fmt, int64_t M, int64_t N, int64_t K, int sms, bool al
     p.ring = smallm2_shape_ok(fmt, M, K) && (opair == 5 || (opair == 0 && M <= kSmallM2AutoMaxM));
     p.bm = M <= 8 ? 8 : 16;
     p.m_tiles = 1;
-    int r16 = smallm_r16(fmt, M, N, sms);
-    if (p.ring) smallm2_config(N, sms, &r16, &p.cps);
+    int r16 = smallm_rows(fmt, M, N, sms, gated);
+    if (p.ring) smallm2_config(N, sms, gated, &r16, &p.cps);
     p.r16 = r16;
     p.n_tiles = static_cast<int>((N + 16 * r16 - 1) / (16 * r16));
     p.tiles = p.n_tiles;
@@ -723,7 +753,7 @@ template <int FMT, int MT>
 static int launch_smallm(DeviceInfo* d, const Plan& p, const void* x, const uint8_t* w,
                          const float* absmax, float scale, const void* bias, void* y, int64_t M,
                          int64_t N, int64_t K, int act, int64_t ldy, cudaStream_t st) {
-  switch (smallm_r16(FMT, M, N, d->sms)) {
+  switch (smallm_rows(FMT, M, N, d->sms, act_is_gated(act))) {
     case 4:
       if constexpr (MT == 1)
         return launch_smallm_cfg<FMT, MT, 4>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
@@ -803,10 +833,17 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
                        void* ws, size_t ws_bytes, cudaStream_t st, const TpOpts* tp = nullptr,
                        bool allow_twophase = true, int act = kActNone, int64_t ldy = 0,
                        size_t max_split_ws = SIZE_MAX) {
-  if (act != kActNone && act != kActGeluTanh) return DQ_ERR_ARG;
-  // y row stride (elements): N unless the caller writes into a wider buffer
-  if (ldy == 0) ldy = N;
-  if (ldy < N || ldy > INT32_MAX || (tp != nullptr && ldy != N)) return DQ_ERR_SHAPE;
+  if (act < kActNone || act > kActGeGluTanh) return DQ_ERR_ARG;
+  const bool gated = act_is_gated(act);
+  // a gated activation takes 32-row groups of the gated row order and writes
+  // N / 2 columns; the column-parallel path has no gated epilogue
+  if (gated && tp != nullptr) return DQ_ERR_ARG;
+  if (gated && (N <= 0 || N % 32 != 0)) return DQ_ERR_SHAPE;
+  const int64_t n_out = gated ? N / 2 : N;
+  // y row stride (elements): the output width unless the caller writes into a
+  // wider buffer
+  if (ldy == 0) ldy = n_out;
+  if (ldy < n_out || ldy > INT32_MAX || (tp != nullptr && ldy != N)) return DQ_ERR_SHAPE;
   // NF4 blocks of 64 must lie inside a weight row; fp8 needs only 16-byte
   // row strides for TMA (the ragged last k-block is zero-filled).
   if (M < 0 || N <= 0 || K <= 0 || (K % (fmt == kFmtNF4 ? 64 : 16)) != 0) return DQ_ERR_SHAPE;
@@ -821,7 +858,7 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
   int rc = current_device(&d);
   if (rc != DQ_OK) return rc;
   const Plan p = make_plan(fmt, M, N, K, d->sms, tp == nullptr, allow_twophase && tp == nullptr,
-                           tp == nullptr, max_split_ws);
+                           tp == nullptr, max_split_ws, gated);
   if (max_split_ws != SIZE_MAX && p.ws > max_split_ws) return DQ_ERR_SCRATCH_LIMIT;
   if (p.ws > 0 && (ws == nullptr || ws_bytes < p.ws || !aligned(ws, 16))) return DQ_ERR_WORKSPACE;
 
@@ -895,7 +932,7 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
     g.n_out = 1;
     g.ldy = static_cast<int>(ldy);
     g.col0 = 0;
-    g.vec_ok = (N % 8 == 0) && (ldy % 8 == 0) && aligned(y, 16);
+    g.vec_ok = (n_out % 8 == 0) && (ldy % 8 == 0) && aligned(y, 16);
     g.tp_counter = nullptr;
     g.tp_rank = 0;
     g.tp_epoch = 0;
@@ -951,7 +988,7 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
     a.n_out = 1;
     a.ldy = static_cast<int>(ldy);
     a.col0 = 0;
-    a.vec_ok = (N % 8 == 0) && (ldy % 8 == 0) && aligned(y, 16);
+    a.vec_ok = (n_out % 8 == 0) && (ldy % 8 == 0) && aligned(y, 16);
   } else {
     a.n_out = tp->world;
     a.ldy = static_cast<int>(N * tp->world);
@@ -975,7 +1012,7 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
   }
   if (rc != DQ_OK) return rc;
   if (p.splits > 1) {
-    const int64_t total = M * N;
+    const int64_t total = M * n_out;
     splitk_reduce_kernel<<<grid_for(total, 256, d->sms), 256, 0, st>>>(
         static_cast<const float*>(ws), p.splits, a.M, a.N, a.bias,
         static_cast<__nv_bfloat16*>(y), a.act, ldy);
@@ -1128,7 +1165,7 @@ size_t dq_workspace_size(int64_t M, int64_t N, int64_t K, int fmt) {
 int dq_linear_nf4_ld(const void* x, int64_t M, int64_t K, const uint8_t* packed,
                      const float* absmax, const void* bias, int64_t N, int act, void* y,
                      int64_t ldy, void* workspace, size_t workspace_bytes, dq_stream_t stream) {
-  if (ldy < N) return DQ_ERR_SHAPE;
+  if (ldy <= 0) return DQ_ERR_SHAPE;  // linear_impl refuses strides below the output width
   return linear_impl(kFmtNF4, x, M, K, packed, absmax, 0.f, bias, N, y, workspace, workspace_bytes,
                      static_cast<cudaStream_t>(stream), nullptr, true, act, ldy);
 }
@@ -1136,7 +1173,7 @@ int dq_linear_nf4_ld(const void* x, int64_t M, int64_t K, const uint8_t* packed,
 int dq_linear_fp8_ld(const void* x, int64_t M, int64_t K, const uint8_t* w8, float scale,
                      const void* bias, int64_t N, int act, void* y, int64_t ldy, void* workspace,
                      size_t workspace_bytes, dq_stream_t stream) {
-  if (ldy < N) return DQ_ERR_SHAPE;
+  if (ldy <= 0) return DQ_ERR_SHAPE;  // linear_impl refuses strides below the output width
   return linear_impl(kFmtFP8, x, M, K, w8, nullptr, scale, bias, N, y, workspace, workspace_bytes,
                      static_cast<cudaStream_t>(stream), nullptr, true, act, ldy);
 }

@@ -308,7 +308,14 @@ __device__ __forceinline__ void dequant_fp8_chunks(const uint4* __restrict__ src
   }
 }
 
-enum : int { kActNone = 0, kActGeluTanh = 1 };
+// Epilogue activations.  The gated ones (SwiGLU: silu(gate) * up, as the
+// FLUX.2 / Z-Image feed-forward, R/dit_flux2_modules.R:77-84; GeGLU-tanh:
+// gelu_tanh(gate) * up) take the weight in the gated row order: per group of
+// 32 weight rows, rows 0-15 are the gate rows of 16 output features and rows
+// 16-31 the up rows of the same features, so y has half as many columns.
+enum : int { kActNone = 0, kActGeluTanh = 1, kActSwiGlu = 2, kActGeGluTanh = 3 };
+
+__host__ __device__ __forceinline__ bool act_is_gated(int act) { return act >= kActSwiGlu; }
 
 // GELU, tanh approximation, in float32: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))),
 // with tanh(u) = 1 - 2 / (exp(2u) + 1) on the exp intrinsic: a few instructions
@@ -329,6 +336,18 @@ __device__ __forceinline__ float gelu_tanh(float x) {
 __device__ __forceinline__ float apply_act(float v, int act) {
   if (act == kActGeluTanh) return gelu_tanh(__bfloat162float(__float2bfloat16_rn(v)));
   return v;
+}
+
+__device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// One output of a gated activation from the f32 sums of its gate and up rows
+// (bias included), rounded as the reference's tensor chain rounds: the
+// projection to bf16, the activation of the bf16 gate to bf16 (SiLU
+// x / (1 + e^-x) in f32, as torch evaluates it), then the bf16 product.
+__device__ __forceinline__ float gated_value(float gate, float up, int act) {
+  const float g = round_bf16(gate);
+  const float a = act == kActSwiGlu ? g / (1.0f + expf(-g)) : gelu_tanh(g);
+  return round_bf16(a) * round_bf16(up);
 }
 
 }  // namespace dq

@@ -411,50 +411,56 @@ __global__ void __launch_bounds__(Gemm2Cfg<FMT, BM>::kThreads, 1)
           // instantiation; the store loop is compiled only there: even an
           // untaken one costs ~10% at BM=256, where the drain is exposed)
           __nv_bfloat16* sb = reinterpret_cast<__nv_bfloat16*>(stg);
-          if (args.act == kActNone) {
-#pragma unroll
-            for (int j = 0; j < EC; ++j)
-              sts16(stg_s + 2u * (j * 32 + lane),
-                    __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(vc[j]) + bias)));
+          if (act_is_gated(args.act)) {
+            gated_chunk_store<EC>(vc, bias, args.act, stg_s, sb,
+                                  reinterpret_cast<__nv_bfloat16*>(args.outs[0]) + args.col0, args.ldy, args.M,
+                                  args.N / 2, mrow0, ncol0 / 2, args.vec_ok, lane);
           } else {
+            if (args.act == kActNone) {
 #pragma unroll
-            for (int j = 0; j < EC; ++j)
-              sts16(stg_s + 2u * (j * 32 + lane),
-                    __bfloat16_as_ushort(__float2bfloat16_rn(
-                        apply_act(__uint_as_float(vc[j]) + bias, args.act))));
-          }
-          __syncwarp();
+              for (int j = 0; j < EC; ++j)
+                sts16(stg_s + 2u * (j * 32 + lane),
+                      __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(vc[j]) + bias)));
+            } else {
 #pragma unroll
-          for (int i = 0; i < EC / 8; ++i) {
-            const int row = (lane >> 2) + 8 * i;
-            const int col = (lane & 3) * 8;
-            const int m = mrow0 + row;
-            const int nc = ncol0 + col;
-            if (m < args.M) {
-              const size_t off = static_cast<size_t>(m) * args.ldy + args.col0 + nc;
-              if (args.vec_ok && nc + 8 <= args.N) {
-                const uint4 v16 = lds128(stg_s + 2u * (row * 32 + col));
-                if constexpr (TP) {
+              for (int j = 0; j < EC; ++j)
+                sts16(stg_s + 2u * (j * 32 + lane),
+                      __bfloat16_as_ushort(__float2bfloat16_rn(
+                          apply_act(__uint_as_float(vc[j]) + bias, args.act))));
+            }
+            __syncwarp();
 #pragma unroll
-                  for (int d = 0; d < kMaxRanks; ++d)
-                    if (d < args.n_out)
-                      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.outs[d]) + off) = v16;
+            for (int i = 0; i < EC / 8; ++i) {
+              const int row = (lane >> 2) + 8 * i;
+              const int col = (lane & 3) * 8;
+              const int m = mrow0 + row;
+              const int nc = ncol0 + col;
+              if (m < args.M) {
+                const size_t off = static_cast<size_t>(m) * args.ldy + args.col0 + nc;
+                if (args.vec_ok && nc + 8 <= args.N) {
+                  const uint4 v16 = lds128(stg_s + 2u * (row * 32 + col));
+                  if constexpr (TP) {
+#pragma unroll
+                    for (int d = 0; d < kMaxRanks; ++d)
+                      if (d < args.n_out)
+                        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.outs[d]) + off) = v16;
+                  } else {
+                    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.outs[0]) + off) = v16;
+                  }
                 } else {
-                  *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.outs[0]) + off) = v16;
-                }
-              } else {
-                const __nv_bfloat16* src = sb + row * 32 + col;
+                  const __nv_bfloat16* src = sb + row * 32 + col;
 #pragma unroll
-                for (int d = 0; d < (TP ? kMaxRanks : 1); ++d) {
-                  if (d >= args.n_out) break;
-                  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.outs[d]) + off;
-                  for (int e = 0; e < 8; ++e)
-                    if (nc + e < args.N) dst[e] = src[e];
+                  for (int d = 0; d < (TP ? kMaxRanks : 1); ++d) {
+                    if (d >= args.n_out) break;
+                    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.outs[d]) + off;
+                    for (int e = 0; e < 8; ++e)
+                      if (nc + e < args.N) dst[e] = src[e];
+                  }
                 }
               }
             }
+            __syncwarp();
           }
-          __syncwarp();
         } else {
           float* sf = reinterpret_cast<float*>(stg);
 #pragma unroll

@@ -212,6 +212,32 @@ __global__ void __launch_bounds__(SmallMCfg<FMT, MT, R16>::kThreads, SmallMCfg<F
       dst[(2 * tig + 1) * 16 + g4 + 8] = acc[rr][mt][3];
     }
   __syncthreads();
+  if (act_is_gated(act)) {
+    // gated row order: row groups 2p (gate) and 2p + 1 (up) give output
+    // features row0 / 2 + 16 p .. +15 (R16 is even here)
+    for (int o = threadIdx.x; o < (R16 / 2) * MT * 128; o += C::kThreads) {
+      const int row = o & 15;
+      const int tok = (o >> 4) & 7;
+      const int pm = o >> 7;  // pair * MT + mt
+      const int pr = pm / MT, mt = pm - pr * MT;
+      float g = 0.f, u = 0.f;
+#pragma unroll
+      for (int wp = 0; wp < C::kWarps; ++wp) {
+        g += red[((wp * R16 + 2 * pr) * MT + mt) * 128 + tok * 16 + row];
+        u += red[((wp * R16 + 2 * pr + 1) * MT + mt) * 128 + tok * 16 + row];
+      }
+      const int64_t ng = row0 + 32 * pr + row;
+      const int m = 8 * mt + tok;
+      if (ng < N && m < M) {
+        if (bias != nullptr) {
+          g += __bfloat162float(bias[ng]);
+          u += __bfloat162float(bias[ng + 16]);
+        }
+        y[static_cast<int64_t>(m) * ldy + row0 / 2 + 16 * pr + row] = __float2bfloat16_rn(gated_value(g, u, act));
+      }
+    }
+    return;
+  }
   // element o = ((rr * MT + mt) * 8 + token) * 16 + row: consecutive threads
   // store consecutive output features of one token
   for (int o = threadIdx.x; o < R16 * MT * 128; o += C::kThreads) {

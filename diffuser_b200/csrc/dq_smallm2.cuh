@@ -268,7 +268,31 @@ __global__ void __launch_bounds__(SmallM2Cfg<FMT, MT, R16, CPS>::kThreads, CPS)
       dst[(2 * tig + 1) * 16 + g4 + 8] = acc[0][mt][3] + acc[1][mt][3];
     }
     asm volatile("bar.sync 1, %0;" ::"n"(32 * C::kConsumerWarps) : "memory");
-    if (!*abort_flag) {
+    if (!*abort_flag && act_is_gated(act)) {
+      // gated row order: row groups 2p (gate) and 2p + 1 (up) of this CTA
+      // give output features row0 / 2 + 16 p .. +15 (R16 is even here)
+      for (int o = threadIdx.x; o < (R16 / 2) * MT * 128; o += 32 * C::kConsumerWarps) {
+        const int row = o & 15;
+        const int tok = (o >> 4) & 7;
+        const int pm = o >> 7;  // pair * MT + mt
+        const int pr = pm / MT, mt = pm - pr * MT;
+        float g = 0.f, u = 0.f;
+#pragma unroll
+        for (int q = 0; q < C::kKgPerStage; ++q) {
+          g += red[((q * R16 + 2 * pr) * MT + mt) * 128 + tok * 16 + row];
+          u += red[((q * R16 + 2 * pr + 1) * MT + mt) * 128 + tok * 16 + row];
+        }
+        const int64_t ng = row0 + 32 * pr + row;  // gate row; its up row is ng + 16
+        const int m = 8 * mt + tok;
+        if (ng < N && m < M) {
+          if (bias != nullptr) {
+            g += __bfloat162float(bias[ng]);
+            u += __bfloat162float(bias[ng + 16]);
+          }
+          y[static_cast<int64_t>(m) * ldy + row0 / 2 + 16 * pr + row] = __float2bfloat16_rn(gated_value(g, u, act));
+        }
+      }
+    } else if (!*abort_flag) {
       // output o = (rg * MT + mt) * 128 + token * 16 + row: consecutive threads
       // store consecutive output features of one token
       for (int o = threadIdx.x; o < R16 * MT * 128; o += 32 * C::kConsumerWarps) {

@@ -38,6 +38,7 @@ class Ltx23Nf4Linear(nn.Module):
             self.bias = nn.Parameter(torch.zeros(out_features))
         else:
             self.register_parameter("bias", None)
+        self.gated_act = None
 
     def set_nf4_weight(self, packed: torch.Tensor, absmax: torch.Tensor):
         """Copy packed codes and block scales into the buffers (R/nf4_ltx23.R:228-234)."""
@@ -52,10 +53,26 @@ class Ltx23Nf4Linear(nn.Module):
             self.weight_absmax = self.weight_absmax.to(torch.float32)
         return self
 
+    def to_gated(self, act: str = "swiglu"):
+        """Reorder the rows of a [gate; up] projection into the gated row
+        order and fuse `act` ("swiglu": silu(gate) * up, "geglu_tanh") into
+        every forward, which then returns out_features / 2 columns."""
+        if act not in ops.GATED_ACTS:
+            raise ValueError(f"act must be one of {ops.GATED_ACTS}")
+        with torch.no_grad():
+            p, a = ops.to_gated_rows_nf4(self.weight_nf4, self.weight_absmax, self.out_features,
+                                         self.in_features)
+            self.weight_nf4.copy_(p)
+            self.weight_absmax.copy_(a)
+            if self.bias is not None:
+                self.bias.copy_(ops.to_gated_rows(self.bias.detach(), self.out_features))
+        self.gated_act = act
+        return self
+
     def forward(self, x: torch.Tensor, act: str | None = None,
                 out: torch.Tensor | None = None) -> torch.Tensor:
         return ops.nf4_linear(x, self.weight_nf4, self.weight_absmax, self.out_features, self.bias,
-                              act=act, out=out)
+                              act=act or self.gated_act, out=out)
 
     def extra_repr(self) -> str:
         return f"in_features={self.in_features}, out_features={self.out_features}, format=nf4"
@@ -82,6 +99,7 @@ class Ltx23Fp8Linear(nn.Module):
             self.bias = nn.Parameter(torch.zeros(out_features))
         else:
             self.register_parameter("bias", None)
+        self.gated_act = None
 
     def set_fp8_weight(self, weight: torch.Tensor, scale, pin: bool = False):
         """Store the e4m3 weight and float32 scale (R/fp8_ltx23.R:60-68)."""
@@ -96,8 +114,24 @@ class Ltx23Fp8Linear(nn.Module):
         self._resident = weight if weight.is_cuda else None
         return self
 
+    def to_gated(self, act: str = "swiglu"):
+        """As Ltx23Nf4Linear.to_gated: rows into the gated row order, `act`
+        fused into every forward (out_features / 2 output columns)."""
+        if act not in ops.GATED_ACTS:
+            raise ValueError(f"act must be one of {ops.GATED_ACTS}")
+        if self.weight_fp8 is None:
+            raise RuntimeError("set_fp8_weight() has not been called")
+        self.weight_fp8 = ops.to_gated_rows(self.weight_fp8, self.out_features)
+        self._resident = self.weight_fp8 if self.weight_fp8.is_cuda else None
+        if self.bias is not None:
+            with torch.no_grad():
+                self.bias.copy_(ops.to_gated_rows(self.bias.detach(), self.out_features))
+        self.gated_act = act
+        return self
+
     def forward(self, x: torch.Tensor, act: str | None = None,
                 out: torch.Tensor | None = None) -> torch.Tensor:
+        act = act or self.gated_act
         if self.weight_fp8 is None:
             raise RuntimeError("set_fp8_weight() has not been called")
         w8 = self._resident
@@ -108,6 +142,31 @@ class Ltx23Fp8Linear(nn.Module):
 
     def extra_repr(self) -> str:
         return f"in_features={self.in_features}, out_features={self.out_features}, format=fp8"
+
+
+class Flux2FeedForward(nn.Module):
+    """flux2_feed_forward (R/dit_flux2_modules.R:73-87) on quantized linears:
+    ``linear_in`` (dim -> 2 * inner, [gate; up]) runs in the gated row order
+    with SiLU(gate) * up fused into its epilogue, then ``linear_out``
+    (inner -> dim_out).  Build it from the reference module's two linears with
+    ``from_linears``; forward(x) returns the same values as
+    linear_out(silu(h[..., :inner]) * h[..., inner:]) with h = linear_in(x)."""
+
+    def __init__(self, linear_in: nn.Module, linear_out: nn.Module):
+        super().__init__()
+        self.linear_in = linear_in
+        self.linear_out = linear_out
+
+    @classmethod
+    def from_linears(cls, linear_in: nn.Linear, linear_out: nn.Linear, fmt: str = "nf4"):
+        holder = nn.Module()
+        holder.linear_in, holder.linear_out = linear_in, linear_out
+        swap_quant_linears(holder, lambda key: True, fmt)
+        holder.linear_in.to_gated("swiglu")
+        return cls(holder.linear_in, holder.linear_out)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return self.linear_out(self.linear_in(x))
 
 
 # Reference-spelled aliases, so callers read like the R API.

@@ -172,7 +172,54 @@ def _prep_bias(bias, n: int, device):
     return b.contiguous()
 
 
-_ACTS = {None: _lib.DQ_ACT_NONE, "gelu_tanh": _lib.DQ_ACT_GELU_TANH}
+_ACTS = {None: _lib.DQ_ACT_NONE, "gelu_tanh": _lib.DQ_ACT_GELU_TANH, "swiglu": _lib.DQ_ACT_SWIGLU,
+         "geglu_tanh": _lib.DQ_ACT_GEGLU_TANH}
+GATED_ACTS = ("swiglu", "geglu_tanh")
+
+
+def _act_code(act, n: int) -> tuple[int, int]:
+    """(C-ABI activation code, output width) of a linear with n weight rows."""
+    if act not in _ACTS:
+        raise ValueError(f"unknown activation {act!r}; expected one of {list(_ACTS)}")
+    if act in GATED_ACTS:
+        if n % 32 != 0:
+            raise ValueError("a gated activation needs out_features % 32 == 0 (gated row order)")
+        return _ACTS[act], n // 2
+    return _ACTS[act], n
+
+
+# ------------------------------------------------------------ gated rows
+def gated_row_order(n: int, device=None) -> torch.Tensor:
+    """Row permutation from the reference's [gate; up] halves of an n-row
+    weight (R/dit_flux2_modules.R:77-84: silu(first half) * second half) to
+    the gated row order of the epilogue: for each block b of 16 output
+    features, rows 32b .. 32b+15 are gate rows 16b .. 16b+15 and rows
+    32b+16 .. 32b+31 the up rows n/2 + 16b .. n/2 + 16b+15."""
+    if n % 32 != 0:
+        raise ValueError("the gated row order needs n % 32 == 0")
+    h = n // 2
+    b = torch.arange(n // 32).view(-1, 1) * 16
+    i = torch.arange(16).view(1, -1)
+    order = torch.stack([b + i, h + b + i], dim=1).reshape(-1)
+    return order if device is None else order.to(device)
+
+
+def to_gated_rows_nf4(packed: torch.Tensor, absmax: torch.Tensor, n: int, k: int):
+    """NF4 buffers of a [gate; up] weight reordered into the gated row order:
+    rows are whole byte ranges of the packed codes and of the block scales
+    (K % 64 == 0), so the reorder is a row gather."""
+    order = gated_row_order(n, packed.device)
+    p = packed.reshape(n, k // 2).index_select(0, order).reshape(-1)
+    a = absmax.reshape(n, k // NF4_BLOCK).index_select(0, order.to(absmax.device)).reshape(-1)
+    return p, a
+
+
+def to_gated_rows(t: torch.Tensor, n: int) -> torch.Tensor:
+    """Rows of an fp8 weight [n, K] (or a bias [n]) in the gated row order."""
+    order = gated_row_order(n, t.device)
+    raw = t.view(torch.uint8) if t.dtype == torch.float8_e4m3fn else t
+    out = raw.index_select(0, order)
+    return out.view(torch.float8_e4m3fn) if t.dtype == torch.float8_e4m3fn else out
 
 
 def _out_rows(out: torch.Tensor, m: int, n: int) -> int:
@@ -193,24 +240,27 @@ def nf4_linear(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor,
                out_features: int, bias: torch.Tensor | None = None, act: str | None = None,
                out: torch.Tensor | None = None) -> torch.Tensor:
     """y = x . dequant_nf4(W)^T + bias (R/nf4_ltx23.R:235-246); act="gelu_tanh"
-    applies GELU-tanh in the epilogue, as gelu_proj does after the projection.
-    With `out` (e.g. a column range of a wider buffer) y is written there."""
+    applies GELU-tanh in the epilogue, as gelu_proj does after the projection;
+    act="swiglu" / "geglu_tanh" gate a weight in the gated row order
+    (to_gated_rows_nf4) and return out_features / 2 columns.  With `out`
+    (e.g. a column range of a wider buffer) y is written there."""
     n = int(out_features)
     k = packed.numel() * 2 // n
+    code, n_out = _act_code(act, n)
     x2 = _prep_x(x, k)
     m = x2.shape[0]
     b = _prep_bias(bias, n, x.device)
     am = absmax if absmax.dtype == torch.float32 else absmax.float()
     if out is not None:
-        ldy = _out_rows(out, m, n)
+        ldy = _out_rows(out, m, n_out)
         with torch.cuda.device(x.device):
             ws_bytes = workspace_size(m, n, k, _lib.DQ_FMT_NF4)
             ws = workspace(x.device, ws_bytes)
             _lib.check("dq_linear_nf4_ld", _lib.lib().dq_linear_nf4_ld(
-                _ptr(x2), m, k, _ptr(packed), _ptr(am), _ptr(b), n, _ACTS[act], _ptr(out), ldy,
+                _ptr(x2), m, k, _ptr(packed), _ptr(am), _ptr(b), n, code, _ptr(out), ldy,
                 _ptr(ws), ws_bytes, _stream(x.device)))
         return out
-    y = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    y = torch.empty((m, n_out), dtype=torch.bfloat16, device=x.device)
     with torch.cuda.device(x.device):
         ws_bytes = workspace_size(m, n, k, _lib.DQ_FMT_NF4)
         ws = workspace(x.device, ws_bytes)
@@ -220,32 +270,35 @@ def nf4_linear(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor,
                 _ptr(ws), ws_bytes, _stream(x.device)))
         else:
             _lib.check("dq_linear_nf4_ex", _lib.lib().dq_linear_nf4_ex(
-                _ptr(x2), m, k, _ptr(packed), _ptr(am), _ptr(b), n, _ACTS[act], _ptr(y),
+                _ptr(x2), m, k, _ptr(packed), _ptr(am), _ptr(b), n, code, _ptr(y),
                 _ptr(ws), ws_bytes, _stream(x.device)))
-    return y.reshape(*x.shape[:-1], n)
+    return y.reshape(*x.shape[:-1], n_out)
 
 
 def fp8_linear(x: torch.Tensor, w8: torch.Tensor, scale: float,
                bias: torch.Tensor | None = None, act: str | None = None,
                out: torch.Tensor | None = None) -> torch.Tensor:
     """y = x . (e4m3(W) * bf16(scale))^T + bias fused (R/fp8_ltx23.R:70-83);
-    act="gelu_tanh" applies GELU-tanh in the epilogue; with `out` y is written
-    there (its rows may be spaced wider than out_features)."""
+    act="gelu_tanh" applies GELU-tanh in the epilogue, act="swiglu" /
+    "geglu_tanh" gate a weight in the gated row order (to_gated_rows) and
+    return half as many columns; with `out` y is written there (its rows may
+    be spaced wider than the output width)."""
     n, k = int(w8.shape[0]), int(w8.shape[1])
+    code, n_out = _act_code(act, n)
     x2 = _prep_x(x, k)
     m = x2.shape[0]
     b = _prep_bias(bias, n, x.device)
     raw = w8.view(torch.uint8)
     if out is not None:
-        ldy = _out_rows(out, m, n)
+        ldy = _out_rows(out, m, n_out)
         with torch.cuda.device(x.device):
             ws_bytes = workspace_size(m, n, k, _lib.DQ_FMT_FP8)
             ws = workspace(x.device, ws_bytes)
             _lib.check("dq_linear_fp8_ld", _lib.lib().dq_linear_fp8_ld(
-                _ptr(x2), m, k, _ptr(raw), ctypes.c_float(float(scale)), _ptr(b), n, _ACTS[act],
+                _ptr(x2), m, k, _ptr(raw), ctypes.c_float(float(scale)), _ptr(b), n, code,
                 _ptr(out), ldy, _ptr(ws), ws_bytes, _stream(x.device)))
         return out
-    y = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    y = torch.empty((m, n_out), dtype=torch.bfloat16, device=x.device)
     with torch.cuda.device(x.device):
         ws_bytes = workspace_size(m, n, k, _lib.DQ_FMT_FP8)
         ws = workspace(x.device, ws_bytes)
@@ -255,9 +308,9 @@ def fp8_linear(x: torch.Tensor, w8: torch.Tensor, scale: float,
                 _ptr(ws), ws_bytes, _stream(x.device)))
         else:
             _lib.check("dq_linear_fp8_ex", _lib.lib().dq_linear_fp8_ex(
-                _ptr(x2), m, k, _ptr(raw), ctypes.c_float(float(scale)), _ptr(b), n, _ACTS[act],
+                _ptr(x2), m, k, _ptr(raw), ctypes.c_float(float(scale)), _ptr(b), n, code,
                 _ptr(y), _ptr(ws), ws_bytes, _stream(x.device)))
-    return y.reshape(*x.shape[:-1], n)
+    return y.reshape(*x.shape[:-1], n_out)
 
 
 def device_error(device=None) -> int:

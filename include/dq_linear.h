@@ -191,8 +191,21 @@ int dq_tp_linear_fp8(const void* x, int64_t M, int64_t K, const uint8_t* w8_shar
  * DQ_ACT_GELU_TANH, y = bf16(gelu_tanh(bf16(x . W^T + bias))).  Replaces the
  * reference's up-projection followed by nnf_gelu(approximate = "tanh")
  * (ltx23_feed_forward's gelu_proj, R/dit_ltx23_modules.R:500-516, and the
- * FLUX single block's proj_mlp, R/dit_flux_modules.R:311). */
-enum { DQ_ACT_NONE = 0, DQ_ACT_GELU_TANH = 1 };
+ * FLUX single block's proj_mlp, R/dit_flux_modules.R:311).
+ *
+ * Gated activations: DQ_ACT_SWIGLU, y = bf16(bf16(silu(g)) * u), replaces the
+ * FLUX.2 / Z-Image feed-forward's linear_in followed by silu of its first
+ * half times its second half (flux2_feed_forward, R/dit_flux2_modules.R:77-84,
+ * and the MLP half of to_qkv_mlp_proj, :148-150); DQ_ACT_GEGLU_TANH, the same
+ * with gelu_tanh(g) (a GELU-gated MLP such as Gemma3's).  g and u are the
+ * bf16-rounded projections of the gate and up rows.  The weight (and bias)
+ * must be in the gated row order: N % 32 == 0 and, for each output feature
+ * block b of 16, weight rows 32b .. 32b+15 are the gate rows 16b .. 16b+15
+ * and rows 32b+16 .. 32b+31 the up rows of the same features (from the
+ * reference's [gate; up] halves: gated row 32b + i = row 16b + i for i < 16,
+ * row N/2 + 16b + i - 16 otherwise).  y then has N / 2 columns (ldy >= N / 2);
+ * the column-parallel entry points take no gated activation (DQ_ERR_ARG). */
+enum { DQ_ACT_NONE = 0, DQ_ACT_GELU_TANH = 1, DQ_ACT_SWIGLU = 2, DQ_ACT_GEGLU_TANH = 3 };
 int dq_linear_nf4_ex(const void* x, int64_t M, int64_t K, const uint8_t* packed,
                      const float* absmax, const void* bias, int64_t N, int act, void* y,
                      void* workspace, size_t workspace_bytes, dq_stream_t stream);
@@ -201,7 +214,8 @@ int dq_linear_fp8_ex(const void* x, int64_t M, int64_t K, const uint8_t* w8, flo
                      size_t workspace_bytes, dq_stream_t stream);
 
 /* The NF4 / fp8 linear with an activation (as the *_ex entry points) writing
- * y[m * ldy + n] (ldy >= N elements): the output can be a column range of a
+ * y[m * ldy + n] (ldy >= the output width: N, or N / 2 with a gated
+ * activation): the output can be a column range of a
  * wider row-major buffer, e.g. one part of a concatenation that the next
  * linear reads whole (no counterpart in the reference, which concatenates
  * tensors with torch_cat).  Everything else as dq_linear_nf4 / dq_linear_fp8. */

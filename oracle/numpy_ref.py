@@ -239,6 +239,28 @@ def fp8_linear_bf16(x_bits, w8, scale, n, k, bias_bits=None) -> np.ndarray:
     return linear_bf16(np.asarray(x_bits).reshape(-1, k), w, bias_bits)
 
 
+def gated_bf16(y_bits, act="swiglu") -> np.ndarray:
+    """The gated activation of a [gate; up] projection in bf16, as the
+    reference's tensor chain rounds it (R/dit_flux2_modules.R:80-83:
+    nnf_silu(x$narrow(-1, 1, half)) * x$narrow(-1, half + 1, half)): the
+    activation of the bf16 gate computed in float32 (SiLU x / (1 + e^-x);
+    for "geglu_tanh" GELU with the tanh approximation) rounded to bf16, then
+    the bf16 product rounded to bf16.  y_bits [M, 2H] -> bits [M, H]."""
+    y = bf16_bits_to_f32(y_bits)
+    h = y.shape[-1] // 2
+    g = y[..., :h].astype(np.float32)
+    u = y[..., h:].astype(np.float32)
+    if act == "swiglu":
+        a = g / (np.float32(1) + np.exp(-g))
+    elif act == "geglu_tanh":
+        a = np.float32(0.5) * g * (np.float32(1) + np.tanh(
+            np.float32(0.7978845608028654) * (g + np.float32(0.044715) * g * g * g)))
+    else:
+        raise ValueError(act)
+    a = bf16_bits_to_f32(f32_to_bf16_bits(a.astype(np.float32)))
+    return f32_to_bf16_bits((a * u).astype(np.float32))
+
+
 def rel_err(y_bits, ref_bits) -> float:
     """max|y - ref| / max|ref| -- the norm used for the 1e-2 GEMM tolerance."""
     y = bf16_bits_to_f32(y_bits).astype(np.float64)
