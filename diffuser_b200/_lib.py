@@ -74,6 +74,11 @@ SIGNATURES = {
     "dq_linear_fp8_ex": (ctypes.c_int, [ctypes.c_void_p, _c_i64, _c_i64, ctypes.c_void_p, ctypes.c_float,
                                         ctypes.c_void_p, _c_i64, ctypes.c_int, ctypes.c_void_p,
                                         ctypes.c_void_p, _c_sz, ctypes.c_void_p]),
+    "dq_linear_nf4_scaled": (ctypes.c_int, [ctypes.c_void_p, _c_i64, _c_i64, ctypes.c_void_p,
+                                            ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, _c_i64,
+                                            ctypes.c_int, ctypes.c_void_p, _c_i64, ctypes.c_void_p,
+                                            _c_sz, ctypes.c_void_p]),
+    "dq_dequant_nf4_scaled": (ctypes.c_int, [_c_p, _c_p, ctypes.c_int, _c_i64, _c_p, _c_p]),
     "dq_plan_info": (ctypes.c_int, [_c_i64, _c_i64, _c_i64, ctypes.c_int] + [ctypes.POINTER(ctypes.c_int)] * 4),
 }
 

@@ -82,7 +82,7 @@ __device__ __forceinline__ void dequant_rows(const GemmArgs& a, int64_t r0, int6
   if constexpr (FMT == kFmtNF4) {
     dequant_nf4_chunks(reinterpret_cast<const uint4*>(a.dq_w), a.absmax,
                        reinterpret_cast<uint4*>(a.dq_out), r0 * K / 32, r1 * K / 32, tid, nthr,
-                       stage);
+                       stage, a.scale_bf16 != 0);
   } else {
     // K % 16 == 0, so rows hold whole chunks
     dequant_fp8_chunks(reinterpret_cast<const uint4*>(a.dq_w),

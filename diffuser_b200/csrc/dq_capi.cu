@@ -31,12 +31,12 @@ namespace dq {
 // loops of dq_codec.cuh; 8 warps x 2 KB of staging per CTA), fp8 with a
 // scalar tail for n % 16.
 __global__ void __launch_bounds__(256)
-    dequant_nf4_kernel(const uint4* __restrict__ packed, const float* __restrict__ absmax,
-                       uint4* __restrict__ out, int64_t n_chunks) {
+    dequant_nf4_kernel(const uint4* __restrict__ packed, const void* __restrict__ absmax,
+                       uint4* __restrict__ out, int64_t n_chunks, int scale_bf16) {
   __shared__ uint4 stage[8][128];
   dequant_nf4_chunks(packed, absmax, out, 0, n_chunks,
                      blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x,
-                     static_cast<int64_t>(gridDim.x) * blockDim.x, stage[threadIdx.x >> 5]);
+                     static_cast<int64_t>(gridDim.x) * blockDim.x, stage[threadIdx.x >> 5], scale_bf16 != 0);
 }
 
 __global__ void __launch_bounds__(256)
@@ -197,7 +197,7 @@ struct DeviceInfo {
   int max_pairs[2][6] = {};     // [fmt][bm]
   std::atomic<int> bf16_smem_set[3][6];    // bf16 pair GEMM, [decoded format + 1][bm]
   int bf16_max_pairs[3][6] = {};
-  std::atomic<int> smallm_set[2][2][3];    // small-M kernel, [fmt][token tiles - 1][row groups 1/2/4]
+  std::atomic<int> smallm_set[3][2][3];    // small-M kernel, [fmt, or 2 = NF4 with bf16 scales][token tiles - 1][row groups 1/2/4]
   std::atomic<int> smallm2_set[2][2][3];   // small-M TMA-ring kernel, [fmt][CTAs per SM - 2][row groups]
 };
 
@@ -728,13 +728,13 @@ struct TpOpts {
 static constexpr unsigned long long kTpWaitNs = 5000000000ull;  // 5 s
 
 // The small-M kernel: one CTA per 16 * R16 weight rows, MT 8-token tiles.
-template <int FMT, int MT, int R16>
-static int launch_smallm_cfg(DeviceInfo* d, const Plan& p, const void* x, const uint8_t* w,
-                             const float* absmax, float scale, const void* bias, void* y,
-                             int64_t M, int64_t N, int64_t K, int act, int64_t ldy, cudaStream_t st) {
+template <int FMT, int MT, int R16, bool SBF>
+static int launch_smallm_kern(DeviceInfo* d, const void* x, const uint8_t* w, const void* absmax,
+                              float scale, const void* bias, void* y, int64_t M, int64_t N, int64_t K,
+                              int act, int64_t ldy, cudaStream_t st) {
   using C = SmallMCfg<FMT, MT, R16>;
-  auto kern = smallm_kernel<FMT, MT, R16>;
-  const int rc = once_per_device(d->smallm_set[FMT][MT - 1][R16 == 4 ? 2 : R16 - 1], [&] {
+  auto kern = smallm_kernel<FMT, MT, R16, SBF>;
+  const int rc = once_per_device(d->smallm_set[SBF ? 2 : FMT][MT - 1][R16 == 4 ? 2 : R16 - 1], [&] {
     return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) ==
                    cudaSuccess
                ? static_cast<int>(DQ_OK)
@@ -749,27 +749,37 @@ static int launch_smallm_cfg(DeviceInfo* d, const Plan& p, const void* x, const 
   return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
 }
 
+template <int FMT, int MT, int R16>
+static int launch_smallm_cfg(DeviceInfo* d, const Plan& p, const void* x, const uint8_t* w,
+                             const void* absmax, int sbf, float scale, const void* bias, void* y,
+                             int64_t M, int64_t N, int64_t K, int act, int64_t ldy, cudaStream_t st) {
+  if constexpr (FMT == kFmtNF4) {
+    if (sbf) return launch_smallm_kern<FMT, MT, R16, true>(d, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
+  }
+  return launch_smallm_kern<FMT, MT, R16, false>(d, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
+}
+
 template <int FMT, int MT>
 static int launch_smallm(DeviceInfo* d, const Plan& p, const void* x, const uint8_t* w,
-                         const float* absmax, float scale, const void* bias, void* y, int64_t M,
+                         const void* absmax, int sbf, float scale, const void* bias, void* y, int64_t M,
                          int64_t N, int64_t K, int act, int64_t ldy, cudaStream_t st) {
   switch (smallm_rows(FMT, M, N, d->sms, act_is_gated(act))) {
     case 4:
       if constexpr (MT == 1)
-        return launch_smallm_cfg<FMT, MT, 4>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
+        return launch_smallm_cfg<FMT, MT, 4>(d, p, x, w, absmax, sbf, scale, bias, y, M, N, K, act, ldy, st);
       break;
     case 2:
-      return launch_smallm_cfg<FMT, MT, 2>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
+      return launch_smallm_cfg<FMT, MT, 2>(d, p, x, w, absmax, sbf, scale, bias, y, M, N, K, act, ldy, st);
   }
-  return launch_smallm_cfg<FMT, MT, 1>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
+  return launch_smallm_cfg<FMT, MT, 1>(d, p, x, w, absmax, sbf, scale, bias, y, M, N, K, act, ldy, st);
 }
 
 // The TMA-ring small-M kernel: one CTA per 16 * R16 weight rows, one 8-token
 // tile, CPS CTAs per SM.
 template <int FMT, int R16, int CPS>
-static int launch_smallm2_cfg(DeviceInfo* d, const void* x, const uint8_t* w, const float* absmax,
-                              float scale, const void* bias, void* y, int64_t M, int64_t N, int64_t K,
-                              int act, int64_t ldy, cudaStream_t st) {
+static int launch_smallm2_cfg(DeviceInfo* d, const void* x, const uint8_t* w, const void* absmax,
+                              float scale, const void* bias, void* y, int64_t M, int64_t N,
+                              int64_t K, int act, int64_t ldy, cudaStream_t st) {
   using C = SmallM2Cfg<FMT, 1, R16, CPS>;
   auto kern = smallm2_kernel<FMT, 1, R16, CPS>;
   const int rc = once_per_device(d->smallm2_set[FMT][CPS - 2][R16 == 4 ? 2 : R16 - 1], [&] {
@@ -810,7 +820,7 @@ static int launch_smallm2_cfg(DeviceInfo* d, const void* x, const uint8_t* w, co
 }
 
 template <int FMT, int CPS>
-static int launch_smallm2_r(DeviceInfo* d, int r16, const void* x, const uint8_t* w, const float* absmax,
+static int launch_smallm2_r(DeviceInfo* d, int r16, const void* x, const uint8_t* w, const void* absmax,
                             float scale, const void* bias, void* y, int64_t M, int64_t N, int64_t K,
                             int act, int64_t ldy, cudaStream_t st) {
   switch (r16) {
@@ -822,17 +832,17 @@ static int launch_smallm2_r(DeviceInfo* d, int r16, const void* x, const uint8_t
 
 template <int FMT>
 static int launch_smallm2(DeviceInfo* d, const Plan& p, const void* x, const uint8_t* w,
-                          const float* absmax, float scale, const void* bias, void* y, int64_t M,
+                          const void* absmax, float scale, const void* bias, void* y, int64_t M,
                           int64_t N, int64_t K, int act, int64_t ldy, cudaStream_t st) {
   return p.cps == 3 ? launch_smallm2_r<FMT, 3>(d, p.r16, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st)
                     : launch_smallm2_r<FMT, 2>(d, p.r16, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
 }
 
 static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8_t* w,
-                       const float* absmax, float scale, const void* bias, int64_t N, void* y,
+                       const void* absmax, float scale, const void* bias, int64_t N, void* y,
                        void* ws, size_t ws_bytes, cudaStream_t st, const TpOpts* tp = nullptr,
                        bool allow_twophase = true, int act = kActNone, int64_t ldy = 0,
-                       size_t max_split_ws = SIZE_MAX) {
+                       size_t max_split_ws = SIZE_MAX, int scale_dtype = DQ_DTYPE_F32) {
   if (act < kActNone || act > kActGeGluTanh) return DQ_ERR_ARG;
   const bool gated = act_is_gated(act);
   // a gated activation takes 32-row groups of the gated row order and writes
@@ -849,9 +859,11 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
   if (M < 0 || N <= 0 || K <= 0 || (K % (fmt == kFmtNF4 ? 64 : 16)) != 0) return DQ_ERR_SHAPE;
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return DQ_ERR_SHAPE;
   if (M == 0) return DQ_OK;
+  if (scale_dtype != DQ_DTYPE_F32 && scale_dtype != DQ_DTYPE_BF16) return DQ_ERR_ARG;
+  const int sbf = (fmt == kFmtNF4 && scale_dtype == DQ_DTYPE_BF16) ? 1 : 0;
   if (x == nullptr || w == nullptr || y == nullptr || (fmt == kFmtNF4 && absmax == nullptr))
     return DQ_ERR_ARG;
-  if (!aligned(x, 16) || !aligned(w, 16) || !aligned(absmax, 4) || !aligned(bias, 2) ||
+  if (!aligned(x, 16) || !aligned(w, 16) || !aligned(absmax, sbf ? 2 : 4) || !aligned(bias, 2) ||
       !aligned(y, 2))
     return DQ_ERR_ALIGN;
   DeviceInfo* d = nullptr;
@@ -862,19 +874,19 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
   if (max_split_ws != SIZE_MAX && p.ws > max_split_ws) return DQ_ERR_SCRATCH_LIMIT;
   if (p.ws > 0 && (ws == nullptr || ws_bytes < p.ws || !aligned(ws, 16))) return DQ_ERR_WORKSPACE;
 
-  if (p.smallm && p.ring && (fmt != kFmtNF4 || aligned(absmax, 16))) {
+  if (p.smallm && p.ring && (fmt != kFmtNF4 || (!sbf && aligned(absmax, 16)))) {
     return fmt == kFmtNF4
                ? launch_smallm2<kFmtNF4>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st)
                : launch_smallm2<kFmtFP8>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
   }
-  // (a ring plan whose NF4 scales are not 16-byte aligned falls through to the
-  // register-stream kernel, which picks its own row groups)
+  // (a ring plan whose NF4 scales are bf16 or not 16-byte aligned falls
+  // through to the register-stream kernel, which picks its own row groups)
   if (p.smallm) {
     if (fmt == kFmtNF4)
-      return p.bm <= 8 ? launch_smallm<kFmtNF4, 1>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st)
-                       : launch_smallm<kFmtNF4, 2>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
-    return p.bm <= 8 ? launch_smallm<kFmtFP8, 1>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st)
-                     : launch_smallm<kFmtFP8, 2>(d, p, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
+      return p.bm <= 8 ? launch_smallm<kFmtNF4, 1>(d, p, x, w, absmax, sbf, scale, bias, y, M, N, K, act, ldy, st)
+                       : launch_smallm<kFmtNF4, 2>(d, p, x, w, absmax, sbf, scale, bias, y, M, N, K, act, ldy, st);
+    return p.bm <= 8 ? launch_smallm<kFmtFP8, 1>(d, p, x, w, absmax, sbf, scale, bias, y, M, N, K, act, ldy, st)
+                     : launch_smallm<kFmtFP8, 2>(d, p, x, w, absmax, sbf, scale, bias, y, M, N, K, act, ldy, st);
   }
 
   if (p.twophase) {
@@ -890,7 +902,7 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
       const int64_t n_elems = N * K;
       if (fmt == kFmtNF4) {
         dequant_nf4_kernel<<<decode_grid(n_elems / 32, d->sms), 256, 0, st>>>(
-            reinterpret_cast<const uint4*>(w), absmax, static_cast<uint4*>(ws), n_elems / 32);
+            reinterpret_cast<const uint4*>(w), absmax, static_cast<uint4*>(ws), n_elems / 32, sbf);
       } else {
         dequant_fp8_kernel<<<decode_grid(n_elems / 16 + 1, d->sms), 256, 0, st>>>(
             w, scale, static_cast<__nv_bfloat16*>(ws), n_elems);
@@ -906,7 +918,8 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
                      CU_TENSOR_MAP_SWIZZLE_128B))
       return DQ_ERR_CUDA;
     GemmArgs g;
-    g.absmax = absmax;
+    g.absmax = static_cast<const float*>(absmax);
+    g.scale_bf16 = sbf;
     g.bias = static_cast<const __nv_bfloat16*>(bias);
     g.out = nullptr;
     g.M = static_cast<int>(M);
@@ -952,7 +965,8 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
     return DQ_ERR_CUDA;
 
   GemmArgs a;
-  a.absmax = absmax;
+  a.absmax = static_cast<const float*>(absmax);
+  a.scale_bf16 = sbf;
   a.bias = static_cast<const __nv_bfloat16*>(bias);
   a.M = static_cast<int>(M);
   a.N = static_cast<int>(N);
@@ -1061,7 +1075,7 @@ extern "C" {
 
 const char* dq_version(void) { return DQ_VERSION_STRING; }
 
-int dq_abi_version(void) { return 1; }
+int dq_abi_version(void) { return 2; }
 
 const char* dq_status_string(int s) {
   switch (s) {
@@ -1136,7 +1150,7 @@ int dq_dequant_nf4(const uint8_t* packed, const float* absmax, int64_t n_elems, 
   if (rc != DQ_OK) return rc;
   const int64_t chunks = n_elems / 32;
   dequant_nf4_kernel<<<decode_grid(chunks, d->sms), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const uint4*>(packed), absmax, static_cast<uint4*>(out_bf16), chunks);
+      reinterpret_cast<const uint4*>(packed), absmax, static_cast<uint4*>(out_bf16), chunks, 0);
   return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
 }
 
@@ -1168,6 +1182,33 @@ int dq_linear_nf4_ld(const void* x, int64_t M, int64_t K, const uint8_t* packed,
   if (ldy <= 0) return DQ_ERR_SHAPE;  // linear_impl refuses strides below the output width
   return linear_impl(kFmtNF4, x, M, K, packed, absmax, 0.f, bias, N, y, workspace, workspace_bytes,
                      static_cast<cudaStream_t>(stream), nullptr, true, act, ldy);
+}
+
+int dq_linear_nf4_scaled(const void* x, int64_t M, int64_t K, const uint8_t* packed,
+                         const void* absmax, int scale_dtype, const void* bias, int64_t N, int act,
+                         void* y, int64_t ldy, void* workspace, size_t workspace_bytes,
+                         dq_stream_t stream) {
+  if (ldy < 0) return DQ_ERR_SHAPE;  // 0: the output width
+  return linear_impl(kFmtNF4, x, M, K, packed, absmax, 0.f, bias, N, y, workspace, workspace_bytes,
+                     static_cast<cudaStream_t>(stream), nullptr, true, act, ldy, SIZE_MAX,
+                     scale_dtype);
+}
+
+int dq_dequant_nf4_scaled(const uint8_t* packed, const void* absmax, int scale_dtype,
+                          int64_t n_elems, void* out_bf16, dq_stream_t stream) {
+  if (scale_dtype != DQ_DTYPE_F32 && scale_dtype != DQ_DTYPE_BF16) return DQ_ERR_ARG;
+  const int sbf = scale_dtype == DQ_DTYPE_BF16 ? 1 : 0;
+  if (n_elems < 0 || (n_elems % 64) != 0) return DQ_ERR_SHAPE;
+  if (n_elems == 0) return DQ_OK;
+  if (packed == nullptr || absmax == nullptr || out_bf16 == nullptr) return DQ_ERR_ARG;
+  if (!aligned(packed, 16) || !aligned(out_bf16, 16) || !aligned(absmax, sbf ? 2 : 4)) return DQ_ERR_ALIGN;
+  DeviceInfo* d = nullptr;
+  int rc = current_device(&d);
+  if (rc != DQ_OK) return rc;
+  const int64_t chunks = n_elems / 32;
+  dequant_nf4_kernel<<<decode_grid(chunks, d->sms), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint4*>(packed), absmax, static_cast<uint4*>(out_bf16), chunks, sbf);
+  return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
 }
 
 int dq_linear_fp8_ld(const void* x, int64_t M, int64_t K, const uint8_t* w8, float scale,

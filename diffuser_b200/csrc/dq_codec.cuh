@@ -152,6 +152,14 @@ __device__ __forceinline__ uint32_t bf16_bits(float v) {
   return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v)));
 }
 
+// Block scale i of an NF4 weight whose scales are f32 (the reference's
+// absmax buffer) or bf16 (repacked at load time: bf16(absmax), the value the
+// forward casts to anyway, so both give the same dequantized weights).
+__device__ __forceinline__ float load_scale(const void* absmax, int64_t i, bool bf16) {
+  return bf16 ? __bfloat162float(__ldg(static_cast<const __nv_bfloat16*>(absmax) + i))
+              : __ldg(static_cast<const float*>(absmax) + i);
+}
+
 // absmax$to(bf16), replicated into both halves.
 __device__ __forceinline__ uint32_t nf4_scale2(float absmax) {
   const uint32_t b = bf16_bits(absmax);
@@ -214,9 +222,10 @@ __device__ __forceinline__ uint8_t f32_to_e4m3(float v) {
 // contiguous bytes; a warp whose 32 chunks straddle c1, or one given no stage
 // (nullptr), stores each chunk directly.
 __device__ __forceinline__ void dequant_nf4_chunks(const uint4* __restrict__ src,
-                                                   const float* __restrict__ absmax,
+                                                   const void* __restrict__ absmax,
                                                    uint4* __restrict__ dst, int64_t c0, int64_t c1,
-                                                   int64_t tid, int64_t nthr, uint4* stage) {
+                                                   int64_t tid, int64_t nthr, uint4* stage,
+                                                   bool scale_bf16 = false) {
   const int lane = threadIdx.x & 31;
   for (int64_t c = c0 + tid; c - lane < c1; c += 4 * nthr) {
     uint4 p[4];
@@ -226,7 +235,7 @@ __device__ __forceinline__ void dequant_nf4_chunks(const uint4* __restrict__ src
       const int64_t cu = c + u * nthr;
       if (cu < c1) {
         p[u] = __ldg(src + cu);
-        am[u] = __ldg(absmax + (cu >> 1));
+        am[u] = load_scale(absmax, cu >> 1, scale_bf16);
       }
     }
 #pragma unroll

@@ -75,7 +75,8 @@ __device__ unsigned long long g_dq_cta_trace[1024][3];
 constexpr int kMaxRanks = 8;  // column-parallel ranks one launch can write to
 
 struct GemmArgs {
-  const float* absmax;        // NF4: [N, K/64] f32 block scales
+  const float* absmax;        // NF4: [N, K/64] block scales, f32 (or bf16: scale_bf16)
+  int scale_bf16;             // NF4: absmax holds bf16 scales
   const __nv_bfloat16* bias;  // [N] or nullptr
   void* out;                  // f32 partials [splits, M, N] when splits > 1
   int M, N, K;
@@ -279,7 +280,7 @@ __device__ __forceinline__ float load_absmax(const GemmArgs& a, const RoundCurso
                                              int KB) {
   const int n = c.tc.n0 + r;
   if (!c.valid || n >= a.N || kb >= c.tc.kb1) return 0.f;
-  return __ldg(a.absmax + static_cast<size_t>(n) * KB + kb);
+  return load_scale(a.absmax, static_cast<int64_t>(n) * KB + kb, a.scale_bf16 != 0);
 }
 
 template <int FMT, int BM, bool TP>

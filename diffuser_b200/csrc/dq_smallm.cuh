@@ -75,8 +75,8 @@ struct RowRun {
   float am;
 };
 
-template <int FMT>
-__device__ __forceinline__ void load_run(RowRun<FMT>& r, const uint8_t* w, const float* absmax,
+template <int FMT, bool SBF>
+__device__ __forceinline__ void load_run(RowRun<FMT>& r, const uint8_t* w, const void* absmax,
                                          int64_t row, bool valid, int K, int g, int tig) {
   if (!valid) {
 #pragma unroll
@@ -87,7 +87,7 @@ __device__ __forceinline__ void load_run(RowRun<FMT>& r, const uint8_t* w, const
   if constexpr (FMT == kFmtNF4) {
     const uint4 v = ld_stream16(w + row * (K / 2) + 64 * g + 16 * tig);
     r.p[0] = v.x; r.p[1] = v.y; r.p[2] = v.z; r.p[3] = v.w;
-    r.am = __ldg(absmax + row * (K / 64) + 2 * g + (tig >> 1));
+    r.am = load_scale(absmax, row * (K / 64) + 2 * g + (tig >> 1), SBF);
   } else {
     const uint8_t* src = w + row * K + 128 * g + 32 * tig;
     const uint4 v0 = ld_stream16(src);
@@ -112,10 +112,11 @@ __device__ __forceinline__ void decode_half(const RowRun<FMT>& r, int h, uint32_
   }
 }
 
-template <int FMT, int MT, int R16>
+// SBF: the NF4 block scales are bf16 (repacked at load time), else f32.
+template <int FMT, int MT, int R16, bool SBF>
 __global__ void __launch_bounds__(SmallMCfg<FMT, MT, R16>::kThreads, SmallMCfg<FMT, MT, R16>::kMinCtas)
     smallm_kernel(const __nv_bfloat16* __restrict__ x, const uint8_t* __restrict__ w,
-                  const float* __restrict__ absmax, float fp8_scale,
+                  const void* __restrict__ absmax, float fp8_scale,
                   const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ y, int M,
                   int N, int K, int act, int64_t ldy) {
   using C = SmallMCfg<FMT, MT, R16>;
@@ -149,7 +150,7 @@ __global__ void __launch_bounds__(SmallMCfg<FMT, MT, R16>::kThreads, SmallMCfg<F
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const int64_t row = row0 + 16 * rr + g4 + 8 * hh;
-        load_run<FMT>(r[rr][hh], w, absmax, row, row < N, K, g, tig);
+        load_run<FMT, SBF>(r[rr][hh], w, absmax, row, row < N, K, g, tig);
       }
   };
   if (PF && warp < KG) load_group(cur, warp);

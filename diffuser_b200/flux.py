@@ -555,26 +555,9 @@ def init_random_(model: nn.Module, seed: int = 0, std: float = 0.02):
 
 
 def concat_nf4_linears(mods):
-    """One NF4 linear whose output features are those of `mods`, in order.
-    NF4 blocks of 64 never straddle a weight row, so a row range's packed codes
-    and block scales are contiguous: concatenating the buffers concatenates
-    the rows, with no repacking.  None unless every module is NF4 with the same
-    in_features."""
-    if not mods or any(not isinstance(m, modules.Ltx23Nf4Linear) for m in mods):
-        return None
-    k = mods[0].in_features
-    if any(m.in_features != k for m in mods):
-        return None
-    dev = mods[0].weight_nf4.device
-    fused = modules.Ltx23Nf4Linear(sum(m.out_features for m in mods), k, bias=False).to(dev)
-    fused.set_nf4_weight(torch.cat([m.weight_nf4 for m in mods]),
-                         torch.cat([m.weight_absmax for m in mods]))
-    if any(m.bias is not None for m in mods):
-        dt = next(m.bias.dtype for m in mods if m.bias is not None)
-        fused.bias = nn.Parameter(torch.cat([
-            m.bias.detach().to(dt) if m.bias is not None
-            else torch.zeros(m.out_features, dtype=dt, device=dev) for m in mods]), requires_grad=False)
-    return fused
+    """modules.concat_nf4_linears: NF4 rows are contiguous byte ranges, so
+    concatenating the buffers concatenates the rows (q/k/v of one stream)."""
+    return modules.concat_nf4_linears(mods)
 
 
 def fuse_qkv_projections(model):

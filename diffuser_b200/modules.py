@@ -34,6 +34,7 @@ class Ltx23Nf4Linear(nn.Module):
         n = self.out_features * self.in_features
         self.register_buffer("weight_nf4", torch.zeros(n // 2, dtype=torch.uint8))
         self.register_buffer("weight_absmax", torch.ones(n // NF4_BLOCK, dtype=torch.float32))
+        self.scales_bf16 = False
         if bias:
             self.bias = nn.Parameter(torch.zeros(out_features))
         else:
@@ -49,8 +50,17 @@ class Ltx23Nf4Linear(nn.Module):
 
     def _apply(self, fn, recurse=True):
         super()._apply(fn, recurse)
-        if self.weight_absmax.dtype != torch.float32:
-            self.weight_absmax = self.weight_absmax.to(torch.float32)
+        want = torch.bfloat16 if getattr(self, "scales_bf16", False) else torch.float32
+        if self.weight_absmax.dtype != want:
+            self.weight_absmax = self.weight_absmax.to(want)
+        return self
+
+    def repack_scales_bf16(self):
+        """Load-time repack of the block scales to bf16 (half the scale
+        bytes).  The forward casts absmax to bf16 before scaling
+        (R/nf4_ltx23.R:97), so the dequantized weights are unchanged."""
+        self.weight_absmax = self.weight_absmax.to(torch.bfloat16)
+        self.scales_bf16 = True
         return self
 
     def to_gated(self, act: str = "swiglu"):
@@ -142,6 +152,43 @@ class Ltx23Fp8Linear(nn.Module):
 
     def extra_repr(self) -> str:
         return f"in_features={self.in_features}, out_features={self.out_features}, format=fp8"
+
+
+def concat_nf4_linears(mods):
+    """One NF4 linear whose output features are those of `mods`, in order.
+    NF4 blocks of 64 never straddle a weight row, so a row range's packed codes
+    and block scales are contiguous: concatenating the buffers concatenates
+    the rows, with no repacking.  None unless every module is NF4 with the same
+    in_features and scale dtype."""
+    if not mods or any(not isinstance(m, Ltx23Nf4Linear) for m in mods):
+        return None
+    k = mods[0].in_features
+    if any(m.in_features != k or m.weight_absmax.dtype != mods[0].weight_absmax.dtype for m in mods):
+        return None
+    dev = mods[0].weight_nf4.device
+    fused = Ltx23Nf4Linear(sum(m.out_features for m in mods), k, bias=False).to(dev)
+    if mods[0].scales_bf16:
+        fused.repack_scales_bf16()
+    fused.set_nf4_weight(torch.cat([m.weight_nf4 for m in mods]),
+                         torch.cat([m.weight_absmax for m in mods]))
+    if any(m.bias is not None for m in mods):
+        dt = next(m.bias.dtype for m in mods if m.bias is not None)
+        fused.bias = nn.Parameter(torch.cat([
+            m.bias.detach().to(dt) if m.bias is not None
+            else torch.zeros(m.out_features, dtype=dt, device=dev) for m in mods]), requires_grad=False)
+    return fused
+
+
+def fuse_gated_pair(gate: nn.Module, up: nn.Module, act: str = "geglu_tanh"):
+    """One NF4 linear computing act(gate(x)) * up(x) with the gate fused into
+    its epilogue (the gated MLP of a Gemma-style text encoder, whose gate_proj
+    and up_proj are separate checkpoint weights, R/quantize_gemma3.R:126-130):
+    the two weights' rows concatenated as [gate; up] and put in the gated row
+    order.  NF4 only (fp8's per-tensor scales differ between the two)."""
+    fused = concat_nf4_linears([gate, up])
+    if fused is None or gate.out_features != up.out_features:
+        raise ValueError("fuse_gated_pair needs two NF4 linears of the same shape")
+    return fused.to_gated(act)
 
 
 class Flux2FeedForward(nn.Module):

@@ -123,6 +123,12 @@ def ltx23_nf4_dequantize(packed: torch.Tensor, absmax: torch.Tensor, shape,
         raise ValueError("packed / absmax sizes do not match shape")
     if out is None:
         out = torch.empty(tuple(shape), dtype=torch.bfloat16, device=packed.device)
+    if absmax.dtype == torch.bfloat16:
+        with torch.cuda.device(packed.device):
+            _lib.check("dq_dequant_nf4_scaled", _lib.lib().dq_dequant_nf4_scaled(
+                _ptr(packed.contiguous()), _ptr(absmax.contiguous()), _lib.DQ_DTYPE_BF16, n,
+                _ptr(out), _stream(packed.device)))
+        return out
     am = absmax if absmax.dtype == torch.float32 else absmax.float()
     with torch.cuda.device(packed.device):
         _lib.check("dq_dequant_nf4", _lib.lib().dq_dequant_nf4(
@@ -250,6 +256,18 @@ def nf4_linear(x: torch.Tensor, packed: torch.Tensor, absmax: torch.Tensor,
     x2 = _prep_x(x, k)
     m = x2.shape[0]
     b = _prep_bias(bias, n, x.device)
+    if absmax.dtype == torch.bfloat16:
+        # block scales repacked to bf16 at load time (bf16(absmax), the value
+        # the forward uses): the dtype-tagged entry point
+        y = out if out is not None else torch.empty((m, n_out), dtype=torch.bfloat16, device=x.device)
+        ldy = _out_rows(y, m, n_out)
+        with torch.cuda.device(x.device):
+            ws_bytes = workspace_size(m, n, k, _lib.DQ_FMT_NF4)
+            ws = workspace(x.device, ws_bytes)
+            _lib.check("dq_linear_nf4_scaled", _lib.lib().dq_linear_nf4_scaled(
+                _ptr(x2), m, k, _ptr(packed), _ptr(absmax), _lib.DQ_DTYPE_BF16, _ptr(b), n, code,
+                _ptr(y), ldy, _ptr(ws), ws_bytes, _stream(x.device)))
+        return y if out is not None else y.reshape(*x.shape[:-1], n_out)
     am = absmax if absmax.dtype == torch.float32 else absmax.float()
     if out is not None:
         ldy = _out_rows(out, m, n_out)

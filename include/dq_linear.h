@@ -226,6 +226,23 @@ int dq_linear_fp8_ld(const void* x, int64_t M, int64_t K, const uint8_t* w8, flo
                      const void* bias, int64_t N, int act, void* y, int64_t ldy, void* workspace,
                      size_t workspace_bytes, dq_stream_t stream);
 
+/* The NF4 linear with the block scales in either dtype: scale_dtype =
+ * DQ_DTYPE_F32 (the reference's absmax buffer, f32 [N*K/64]) or DQ_DTYPE_BF16
+ * (the same scales repacked at load time as bf16(absmax): the forward casts
+ * absmax to bf16 before multiplying (R/nf4_ltx23.R:97, R/jit_ltx23.R:49),
+ * so the dequantized weights are bit-identical, with 2 bytes per block
+ * instead of 4).  act and ldy as dq_linear_nf4_ld (ldy = 0: the output width).
+ * Replaces ltx23_nf4_linear$forward (R/nf4_ltx23.R:235-246). */
+int dq_linear_nf4_scaled(const void* x, int64_t M, int64_t K, const uint8_t* packed,
+                         const void* absmax, int scale_dtype, const void* bias, int64_t N, int act,
+                         void* y, int64_t ldy, void* workspace, size_t workspace_bytes,
+                         dq_stream_t stream);
+
+/* NF4 -> bf16 with f32 or bf16 block scales (as dq_linear_nf4_scaled);
+ * replaces ltx23_nf4_dequantize (R/nf4_ltx23.R:77-115), bit-exact. */
+int dq_dequant_nf4_scaled(const uint8_t* packed, const void* absmax, int scale_dtype,
+                          int64_t n_elems, void* out_bf16, dq_stream_t stream);
+
 /* Describes the launch plan dq_linear_* uses for this shape on the current
  * device: *pair = 0 for fused one-CTA tiles (128 weight rows), 1 for fused
  * CTA-pair tiles (256 rows), 2 for the two-phase plan (the bf16 CTA-pair GEMM

@@ -44,7 +44,7 @@ def test_library_exports_every_header_symbol(lib):
 
 def test_version_and_status_strings(lib):
     assert "sm_100a" in _lib.version()
-    assert lib.dq_abi_version() == 1
+    assert lib.dq_abi_version() == 2
     assert _lib.status_string(0) == "ok"
     assert "shape" in _lib.status_string(1)
 

@@ -417,3 +417,30 @@ def test_output_into_column_range(ops, fmt, mode, splits, m):
         ops.set_pair_mode(0)
     assert torch.equal(buf[:, c0:c0 + n], plain)
     assert (buf[:, :c0] == 7.0).all() and (buf[:, c0 + n:] == 7.0).all()
+
+
+@pytest.mark.parametrize("mode,bm,splits,m", [(1, 128, 0, 300), (2, 192, 0, 300), (3, 256, 0, 1100),
+                                              (4, 256, 0, 300), (1, 0, 3, 16), (5, 0, 0, 4),
+                                              (6, 0, 0, 12)])
+def test_bf16_block_scales_give_the_same_bits(ops, mode, bm, splits, m):
+    # scales repacked to bf16 at load time (dq_linear_nf4_scaled): the forward
+    # casts absmax to bf16 anyway, so every plan returns the same bits
+    n, k = 640, 1024
+    x, (p, a), bias, ref = _case(m, n, k, 61 + m, "nf4", with_bias=True)
+    a16 = a.to(torch.bfloat16)
+    xc, bc = x.cuda(), bias.cuda()
+    ops.set_pair_mode(mode)
+    ops.set_tile_override(bm, splits)
+    try:
+        y32 = ops.nf4_linear(xc, p, a, n, bc)
+        y16 = ops.nf4_linear(xc, p, a16, n, bc)
+        torch.cuda.synchronize()
+    finally:
+        ops.set_tile_override(0, 0)
+        ops.set_pair_mode(0)
+    assert torch.equal(y32, y16)
+    assert R.rel_err(to_bits(y16), ref) <= TOL
+    w32 = ops.ltx23_nf4_dequantize(p, a, (n, k))
+    w16 = ops.ltx23_nf4_dequantize(p, a16, (n, k))
+    assert torch.equal(w32, w16)
+    assert ops.device_error() == 0
