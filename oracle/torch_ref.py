@@ -89,7 +89,7 @@ def nf4_lin(x, packed, absmax, bias, table2):
     rows = bias.size(0)
     vals = torch.embedding(table2, packed.int())
     w = vals.reshape([-1, 64]) * absmax.type_as(table2).unsqueeze(1)
-    return torch.linear(x, w.reshape([rows, -1]).type_as(x), bias)
+    return torch.nn.functional.linear(x, w.reshape([rows, -1]).type_as(x), bias)
 
 
 def nf4_linear_forward(x, packed, absmax, n, k, bias=None, w_buffer=None):
@@ -114,3 +114,18 @@ def fp8_linear_forward(x, w8, scale, bias=None, w_buffer=None):
         w.copy_(w8)
         w.mul_(scale.to(device=x.device, dtype=x.dtype))
     return torch.nn.functional.linear(x, w, bias)
+
+
+# TorchScript source of nf4_lin (R/jit_ltx23.R:40-50) and of the linear
+# followed by GELU-tanh (R/jit_ltx23.R:97-99), for compiling the block stack
+# with the reference's own linear as the comparison.
+NF4_LIN_TS_SOURCE = '''
+def REF_LIN(x: Tensor, packed: Tensor, absmax: Tensor, bias: Tensor, table2: Tensor) -> Tensor:
+    rows = bias.size(0)
+    vals = torch.embedding(table2, packed.int())
+    w = vals.reshape([-1, 64]) * absmax.type_as(table2).unsqueeze(1)
+    return torch.nn.functional.linear(x, w.reshape([rows, -1]).type_as(x), bias)
+
+def LIN_GELU_FN(x: Tensor, packed: Tensor, absmax: Tensor, bias: Tensor, table2: Tensor) -> Tensor:
+    return torch.nn.functional.gelu(REF_LIN(x, packed, absmax, bias, table2), approximate="tanh")
+'''
