@@ -192,9 +192,10 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits,
 struct DeviceInfo {
   std::atomic<int> ok;  // 1 = probed
   int major = 0, minor = 0, sms = 0;
-  std::atomic<int> smem_set[2][2][6];   // [column-parallel][fmt][bm]
-  std::atomic<int> smem_set2[2][2][6];
-  int max_pairs[2][6] = {};     // [fmt][bm]
+  // fused kernels, [variant: plain, column-parallel, gated][fmt][bm]
+  std::atomic<int> smem_set[3][2][6];
+  std::atomic<int> smem_set2[3][2][6];
+  int max_pairs[3][2][6] = {};
   std::atomic<int> bf16_smem_set[3][6];    // bf16 pair GEMM, [decoded format + 1][bm]
   int bf16_max_pairs[3][6] = {};
   std::atomic<int> smallm_set[3][2][3];    // small-M kernel, [fmt, or 2 = NF4 with bf16 scales][token tiles - 1][row groups 1/2/4]
@@ -512,13 +513,13 @@ static Plan make_plan(int fmt, int64_t M, int64_t N, int64_t K, int sms, bool al
   return p;
 }
 
-template <int FMT, int BM, bool TP>
+template <int FMT, int BM, int VAR>
 static int launch_gemm(DeviceInfo* d, const Plan& p, const CUtensorMap& mx, const CUtensorMap& mw,
                        const GemmArgs& a, cudaStream_t st) {
   using C = GemmCfg<FMT, BM>;
-  auto kern = dq_gemm_kernel<FMT, BM, TP>;
+  auto kern = dq_gemm_kernel<FMT, BM, VAR>;
   const int bi = bm_index(BM);
-  const int rc = once_per_device(d->smem_set[TP][FMT][bi], [&] {
+  const int rc = once_per_device(d->smem_set[VAR][FMT][bi], [&] {
     return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) ==
                    cudaSuccess
                ? static_cast<int>(DQ_OK)
@@ -532,12 +533,12 @@ static int launch_gemm(DeviceInfo* d, const Plan& p, const CUtensorMap& mx, cons
 // One-time setup of a pair-kernel instantiation on this device: shared-memory
 // opt-in and the number of two-CTA clusters that can be resident at once
 // (cached in d->max_pairs; the persistent grid never exceeds it).
-template <int FMT, int BM, bool TP>
+template <int FMT, int BM, int VAR>
 static int pair_setup(DeviceInfo* d, cudaLaunchConfig_t& cfg) {
   using C = Gemm2Cfg<FMT, BM>;
-  auto kern = dq_gemm2_kernel<FMT, BM, TP>;
+  auto kern = dq_gemm2_kernel<FMT, BM, VAR>;
   const int bi = bm_index(BM);
-  return once_per_device(d->smem_set2[TP][FMT][bi], [&] {
+  return once_per_device(d->smem_set2[VAR][FMT][bi], [&] {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
         cudaSuccess)
       return static_cast<int>(DQ_ERR_LAUNCH);
@@ -545,7 +546,7 @@ static int pair_setup(DeviceInfo* d, cudaLaunchConfig_t& cfg) {
     cfg.gridDim = dim3(2 * std::max(1, d->sms / 2));
     if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1)
       return static_cast<int>(DQ_ERR_LAUNCH);
-    d->max_pairs[FMT][bi] = clusters;
+    d->max_pairs[VAR][FMT][bi] = clusters;
     return static_cast<int>(DQ_OK);
   });
 }
@@ -566,15 +567,15 @@ static cudaLaunchConfig_t pair_config(cudaLaunchAttribute* attr, cudaStream_t st
   return cfg;
 }
 
-template <int FMT, int BM, bool TP>
+template <int FMT, int BM, int VAR>
 static int launch_gemm2(DeviceInfo* d, const Plan& p, const CUtensorMap& mx, const CUtensorMap& mw,
                         const GemmArgs& a, cudaStream_t st) {
-  auto kern = dq_gemm2_kernel<FMT, BM, TP>;
+  auto kern = dq_gemm2_kernel<FMT, BM, VAR>;
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = pair_config<FMT, BM>(attr, st);
-  const int rc = pair_setup<FMT, BM, TP>(d, cfg);
+  const int rc = pair_setup<FMT, BM, VAR>(d, cfg);
   if (rc != DQ_OK) return rc;
-  const int pairs = std::max(1, std::min(p.grid, d->max_pairs[FMT][bm_index(BM)]));
+  const int pairs = std::max(1, std::min(p.grid, d->max_pairs[VAR][FMT][bm_index(BM)]));
   cfg.gridDim = dim3(2 * pairs);
   if (cudaLaunchKernelEx(&cfg, kern, mx, mw, a) != cudaSuccess) return DQ_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
@@ -586,12 +587,12 @@ static int pair_capacity(DeviceInfo* d, int bm, int* pairs) {
   cudaLaunchAttribute attr[1];
   int rc = DQ_ERR_ARG;
   switch (bm) {
-    case 64: { auto c = pair_config<FMT, 64>(attr, nullptr); rc = pair_setup<FMT, 64, false>(d, c); break; }
-    case 128: { auto c = pair_config<FMT, 128>(attr, nullptr); rc = pair_setup<FMT, 128, false>(d, c); break; }
-    case 192: { auto c = pair_config<FMT, 192>(attr, nullptr); rc = pair_setup<FMT, 192, false>(d, c); break; }
-    case 256: { auto c = pair_config<FMT, 256>(attr, nullptr); rc = pair_setup<FMT, 256, false>(d, c); break; }
+    case 64: { auto c = pair_config<FMT, 64>(attr, nullptr); rc = pair_setup<FMT, 64, 0>(d, c); break; }
+    case 128: { auto c = pair_config<FMT, 128>(attr, nullptr); rc = pair_setup<FMT, 128, 0>(d, c); break; }
+    case 192: { auto c = pair_config<FMT, 192>(attr, nullptr); rc = pair_setup<FMT, 192, 0>(d, c); break; }
+    case 256: { auto c = pair_config<FMT, 256>(attr, nullptr); rc = pair_setup<FMT, 256, 0>(d, c); break; }
   }
-  if (rc == DQ_OK) *pairs = d->max_pairs[FMT][bm_index(bm)];
+  if (rc == DQ_OK) *pairs = d->max_pairs[0][FMT][bm_index(bm)];
   return rc;
 }
 
@@ -682,25 +683,25 @@ static int launch_bf16_gemm2_bm(DeviceInfo* d, const Plan& p, const CUtensorMap&
   return DQ_ERR_ARG;
 }
 
-template <int FMT, bool TP>
+template <int FMT, int VAR>
 static int dispatch_gemm(DeviceInfo* d, const Plan& p, const CUtensorMap& mx, const CUtensorMap& mw,
                          const GemmArgs& a, cudaStream_t st) {
   if (p.pair) {
     switch (p.bm) {
-      case 64: return launch_gemm2<FMT, 64, TP>(d, p, mx, mw, a, st);
-      case 128: return launch_gemm2<FMT, 128, TP>(d, p, mx, mw, a, st);
-      case 192: return launch_gemm2<FMT, 192, TP>(d, p, mx, mw, a, st);
-      case 256: return launch_gemm2<FMT, 256, TP>(d, p, mx, mw, a, st);
+      case 64: return launch_gemm2<FMT, 64, VAR>(d, p, mx, mw, a, st);
+      case 128: return launch_gemm2<FMT, 128, VAR>(d, p, mx, mw, a, st);
+      case 192: return launch_gemm2<FMT, 192, VAR>(d, p, mx, mw, a, st);
+      case 256: return launch_gemm2<FMT, 256, VAR>(d, p, mx, mw, a, st);
     }
     return DQ_ERR_ARG;
   }
   switch (p.bm) {
-    case 16: return launch_gemm<FMT, 16, TP>(d, p, mx, mw, a, st);
-    case 32: return launch_gemm<FMT, 32, TP>(d, p, mx, mw, a, st);
-    case 64: return launch_gemm<FMT, 64, TP>(d, p, mx, mw, a, st);
-    case 128: return launch_gemm<FMT, 128, TP>(d, p, mx, mw, a, st);
-    case 192: return launch_gemm<FMT, 192, TP>(d, p, mx, mw, a, st);
-    case 256: return launch_gemm<FMT, 256, TP>(d, p, mx, mw, a, st);
+    case 16: return launch_gemm<FMT, 16, VAR>(d, p, mx, mw, a, st);
+    case 32: return launch_gemm<FMT, 32, VAR>(d, p, mx, mw, a, st);
+    case 64: return launch_gemm<FMT, 64, VAR>(d, p, mx, mw, a, st);
+    case 128: return launch_gemm<FMT, 128, VAR>(d, p, mx, mw, a, st);
+    case 192: return launch_gemm<FMT, 192, VAR>(d, p, mx, mw, a, st);
+    case 256: return launch_gemm<FMT, 256, VAR>(d, p, mx, mw, a, st);
   }
   return DQ_ERR_ARG;
 }
@@ -1017,12 +1018,16 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
     a.tp_rank = tp->rank;
     a.tp_epoch = tp->epoch;
   }
-  if (tp == nullptr) {
-    rc = fmt == kFmtNF4 ? dispatch_gemm<kFmtNF4, false>(d, p, mx, mw, a, st)
-                        : dispatch_gemm<kFmtFP8, false>(d, p, mx, mw, a, st);
+  if (tp != nullptr) {
+    rc = fmt == kFmtNF4 ? dispatch_gemm<kFmtNF4, 1>(d, p, mx, mw, a, st)
+                        : dispatch_gemm<kFmtFP8, 1>(d, p, mx, mw, a, st);
+  } else if (gated && p.splits == 1) {
+    rc = fmt == kFmtNF4 ? dispatch_gemm<kFmtNF4, 2>(d, p, mx, mw, a, st)
+                        : dispatch_gemm<kFmtFP8, 2>(d, p, mx, mw, a, st);
   } else {
-    rc = fmt == kFmtNF4 ? dispatch_gemm<kFmtNF4, true>(d, p, mx, mw, a, st)
-                        : dispatch_gemm<kFmtFP8, true>(d, p, mx, mw, a, st);
+    // (split-K partials are written raw; the reduce kernel applies the gate)
+    rc = fmt == kFmtNF4 ? dispatch_gemm<kFmtNF4, 0>(d, p, mx, mw, a, st)
+                        : dispatch_gemm<kFmtFP8, 0>(d, p, mx, mw, a, st);
   }
   if (rc != DQ_OK) return rc;
   if (p.splits > 1) {

@@ -283,11 +283,17 @@ __device__ __forceinline__ float load_absmax(const GemmArgs& a, const RoundCurso
   return load_scale(a.absmax, static_cast<int64_t>(n) * KB + kb, a.scale_bf16 != 0);
 }
 
-template <int FMT, int BM, bool TP>
+// VAR: 0 = plain epilogue (no activation or GELU-tanh), 1 = column-parallel
+// (every rank's y, then the completion flags), 2 = gated epilogue (SwiGLU /
+// GeGLU-tanh; its own instantiation, which keeps the extra epilogue code out
+// of the other two: compiled into the plain kernel it cost 4-7% at M = 512).
+template <int FMT, int BM, int VAR>
 __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
     dq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x,
                    const __grid_constant__ CUtensorMap tmap_w, const GemmArgs args) {
   using C = GemmCfg<FMT, BM>;
+  constexpr bool TP = VAR == 1;
+  constexpr bool GATED = VAR == 2;
   constexpr int R = C::kRound;
   constexpr int XR = C::kXRounds;
   constexpr int AR = C::kARounds;
@@ -618,7 +624,7 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
           // instantiation; the store loop is compiled only there: even an
           // untaken one costs ~10% at BM=256, where the drain is exposed)
           __nv_bfloat16* sb = reinterpret_cast<__nv_bfloat16*>(stg);
-          if (act_is_gated(args.act)) {
+          if constexpr (GATED) {
             gated_chunk_store<EC>(vc, bias, args.act, stg_s, sb,
                                   reinterpret_cast<__nv_bfloat16*>(args.outs[0]) + args.col0, args.ldy, args.M,
                                   args.N / 2, mrow0, ncol0 / 2, args.vec_ok, lane);

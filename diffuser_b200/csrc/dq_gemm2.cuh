@@ -80,11 +80,17 @@ struct Gemm2Cfg {
   static constexpr uint32_t kXTxBytes = BM * 128;               // both halves of a k-block
 };
 
-template <int FMT, int BM, bool TP>
+// VAR: 0 = plain epilogue (no activation or GELU-tanh), 1 = column-parallel
+// (every rank's y, then the completion flags), 2 = gated epilogue (SwiGLU /
+// GeGLU-tanh; its own instantiation, which keeps the extra epilogue code out
+// of the other two: compiled into the plain kernel it cost 4-7% at M = 512).
+template <int FMT, int BM, int VAR>
 __global__ void __launch_bounds__(Gemm2Cfg<FMT, BM>::kThreads, 1)
     dq_gemm2_kernel(const __grid_constant__ CUtensorMap tmap_x,
                     const __grid_constant__ CUtensorMap tmap_w, const GemmArgs args) {
   using C = Gemm2Cfg<FMT, BM>;
+  constexpr bool TP = VAR == 1;
+  constexpr bool GATED = VAR == 2;
   constexpr int R = C::kRound;
   constexpr int XR = C::kXRounds;
   constexpr int AR = C::kARounds;
@@ -411,7 +417,7 @@ __global__ void __launch_bounds__(Gemm2Cfg<FMT, BM>::kThreads, 1)
           // instantiation; the store loop is compiled only there: even an
           // untaken one costs ~10% at BM=256, where the drain is exposed)
           __nv_bfloat16* sb = reinterpret_cast<__nv_bfloat16*>(stg);
-          if (act_is_gated(args.act)) {
+          if constexpr (GATED) {
             gated_chunk_store<EC>(vc, bias, args.act, stg_s, sb,
                                   reinterpret_cast<__nv_bfloat16*>(args.outs[0]) + args.col0, args.ldy, args.M,
                                   args.N / 2, mrow0, ncol0 / 2, args.vec_ok, lane);
