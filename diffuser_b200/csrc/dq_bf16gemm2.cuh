@@ -92,7 +92,11 @@ __device__ __forceinline__ void dequant_rows(const GemmArgs& a, int64_t r0, int6
   }
 }
 
-template <int BM, int FMT = -1>
+// TP: the column-parallel instantiation -- every output row segment goes to
+// every rank's y (args.outs, column offset args.col0, possibly peer memory),
+// and after the teardown the CTAs count themselves done and the last raises
+// this rank's completion flag on every rank (tp_signal_done).
+template <int BM, int FMT = -1, bool TP = false>
 __global__ void __launch_bounds__(Bf16PairCfg<BM, FMT>::kThreads, 1)
     bf16_gemm2_kernel(const __grid_constant__ CUtensorMap tmap_x,
                       const __grid_constant__ CUtensorMap tmap_a, const GemmArgs args) {
@@ -310,7 +314,6 @@ __global__ void __launch_bounds__(Bf16PairCfg<BM, FMT>::kThreads, 1)
                         apply_act(__uint_as_float(vc[j]) + bias, args.act))));
           }
           __syncwarp();
-          __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(args.outs[0]);
 #pragma unroll
           for (int i = 0; i < EC / 8; ++i) {
             const int row = (lane >> 2) + 8 * i;
@@ -318,13 +321,22 @@ __global__ void __launch_bounds__(Bf16PairCfg<BM, FMT>::kThreads, 1)
             const int m = mrow0 + row;
             const int nc = ncol0 + col;
             if (m < args.M) {
-              __nv_bfloat16* dst = y + static_cast<size_t>(m) * args.ldy + nc;
+              const size_t off = static_cast<size_t>(m) * args.ldy + args.col0 + nc;
               if (args.vec_ok && nc + 8 <= args.N) {
-                *reinterpret_cast<uint4*>(dst) = lds128(stg_s + 2u * (row * 32 + col));
+                const uint4 v16 = lds128(stg_s + 2u * (row * 32 + col));
+#pragma unroll
+                for (int d = 0; d < (TP ? kMaxRanks : 1); ++d)
+                  if (d < args.n_out)
+                    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.outs[d]) + off) = v16;
               } else {
                 const __nv_bfloat16* src = sb + row * 32 + col;
-                for (int e = 0; e < 8; ++e)
-                  if (nc + e < args.N) dst[e] = src[e];
+#pragma unroll
+                for (int d = 0; d < (TP ? kMaxRanks : 1); ++d) {
+                  if (d >= args.n_out) break;
+                  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.outs[d]) + off;
+                  for (int e = 0; e < 8; ++e)
+                    if (nc + e < args.N) dst[e] = src[e];
+                }
               }
             }
           }
@@ -333,6 +345,9 @@ __global__ void __launch_bounds__(Bf16PairCfg<BM, FMT>::kThreads, 1)
       }
       if (++acc == C::kNumAcc) { acc = 0; accphase ^= 1u; }
     }
+    // column-parallel: this thread's peer stores are visible system-wide
+    // before its CTA counts itself done
+    if constexpr (TP) __threadfence_system();
   }
 
   // ------------------------------------------------------------- teardown
@@ -342,6 +357,7 @@ __global__ void __launch_bounds__(Bf16PairCfg<BM, FMT>::kThreads, 1)
   tc_fence_after();
   if (warp == C::kMmaWarp) tmem_dealloc_pair(tmem_base, 512);
   if (threadIdx.x == 0 && *abort_flag) atomicOr(&g_dq_error, 1u << kErrTimeout);
+  if constexpr (TP) tp_signal_done(args);
 }
 
 }  // namespace dq

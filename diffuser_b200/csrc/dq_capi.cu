@@ -196,8 +196,9 @@ struct DeviceInfo {
   std::atomic<int> smem_set[3][2][6];
   std::atomic<int> smem_set2[3][2][6];
   int max_pairs[3][2][6] = {};
-  std::atomic<int> bf16_smem_set[3][6];    // bf16 pair GEMM, [decoded format + 1][bm]
-  int bf16_max_pairs[3][6] = {};
+  // bf16 pair GEMM, [column-parallel][decoded format + 1][bm]
+  std::atomic<int> bf16_smem_set[2][3][6];
+  int bf16_max_pairs[2][3][6] = {};
   std::atomic<int> smallm_set[3][2][3];    // small-M kernel, [fmt, or 2 = NF4 with bf16 scales][token tiles - 1][row groups 1/2/4]
   std::atomic<int> smallm2_set[2][2][3];   // small-M TMA-ring kernel, [fmt][CTAs per SM - 2][row groups]
 };
@@ -614,12 +615,12 @@ static cudaLaunchConfig_t bf16_pair_config(cudaLaunchAttribute* attr, cudaStream
 
 // One-time setup of a bf16 pair GEMM instantiation: shared-memory opt-in and
 // the resident-cluster capacity (cached in d->bf16_max_pairs).
-template <int BM, int FMT>
+template <int BM, int FMT, bool TP = false>
 static int bf16_pair_setup(DeviceInfo* d) {
   using C = Bf16PairCfg<BM, FMT>;
   const int bi = bm_index(BM);
-  return once_per_device(d->bf16_smem_set[FMT + 1][bi], [&] {
-    auto kern = bf16_gemm2_kernel<BM, FMT>;
+  return once_per_device(d->bf16_smem_set[TP][FMT + 1][bi], [&] {
+    auto kern = bf16_gemm2_kernel<BM, FMT, TP>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
         cudaSuccess)
       return static_cast<int>(DQ_ERR_LAUNCH);
@@ -629,7 +630,7 @@ static int bf16_pair_setup(DeviceInfo* d) {
     int clusters = 0;
     if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1)
       return static_cast<int>(DQ_ERR_LAUNCH);
-    d->bf16_max_pairs[FMT + 1][bi] = clusters;
+    d->bf16_max_pairs[TP][FMT + 1][bi] = clusters;
     return static_cast<int>(DQ_OK);
   });
 }
@@ -643,7 +644,7 @@ static int bf16_pair_capacity(DeviceInfo* d, int bm, int* pairs) {
     case 192: rc = bf16_pair_setup<192, FMT>(d); break;
     case 256: rc = bf16_pair_setup<256, FMT>(d); break;
   }
-  if (rc == DQ_OK) *pairs = d->bf16_max_pairs[FMT + 1][bm_index(bm)];
+  if (rc == DQ_OK) *pairs = d->bf16_max_pairs[0][FMT + 1][bm_index(bm)];
   return rc;
 }
 
@@ -652,33 +653,33 @@ static int bf16_pair_capacity(DeviceInfo* d, int bm, int* pairs) {
 // there.  Every CTA must be resident at once (the producers wait for the
 // decode warps of all CTAs): the grid never exceeds the occupancy-derived
 // number of resident pairs.
-template <int BM, int FMT>
+template <int BM, int FMT, bool TP = false>
 static int launch_bf16_gemm2(DeviceInfo* d, const Plan& p, const CUtensorMap& mx,
                              const CUtensorMap& ma, const GemmArgs& a, cudaStream_t st) {
-  const int rc = bf16_pair_setup<BM, FMT>(d);
+  const int rc = bf16_pair_setup<BM, FMT, TP>(d);
   if (rc != DQ_OK) return rc;
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = bf16_pair_config<BM, FMT>(attr, st);
-  const int pairs = std::max(1, std::min(p.grid, d->bf16_max_pairs[FMT + 1][bm_index(BM)]));
+  const int pairs = std::max(1, std::min(p.grid, d->bf16_max_pairs[TP][FMT + 1][bm_index(BM)]));
   cfg.gridDim = dim3(2 * pairs);
   GemmArgs g = a;
   if (FMT >= 0) {
     const int m_tiles = std::max(1, p.m_tiles);
     g.group0_n = std::min(a.group_n, std::max(1, (pairs + m_tiles - 1) / m_tiles));
   }
-  if (cudaLaunchKernelEx(&cfg, bf16_gemm2_kernel<BM, FMT>, mx, ma, g) != cudaSuccess)
+  if (cudaLaunchKernelEx(&cfg, bf16_gemm2_kernel<BM, FMT, TP>, mx, ma, g) != cudaSuccess)
     return DQ_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
 }
 
-template <int FMT>
+template <int FMT, bool TP = false>
 static int launch_bf16_gemm2_bm(DeviceInfo* d, const Plan& p, const CUtensorMap& mx,
                                 const CUtensorMap& ma, const GemmArgs& a, cudaStream_t st) {
   switch (p.bm) {
-    case 64: return launch_bf16_gemm2<64, FMT>(d, p, mx, ma, a, st);
-    case 128: return launch_bf16_gemm2<128, FMT>(d, p, mx, ma, a, st);
-    case 192: return launch_bf16_gemm2<192, FMT>(d, p, mx, ma, a, st);
-    case 256: return launch_bf16_gemm2<256, FMT>(d, p, mx, ma, a, st);
+    case 64: return launch_bf16_gemm2<64, FMT, TP>(d, p, mx, ma, a, st);
+    case 128: return launch_bf16_gemm2<128, FMT, TP>(d, p, mx, ma, a, st);
+    case 192: return launch_bf16_gemm2<192, FMT, TP>(d, p, mx, ma, a, st);
+    case 256: return launch_bf16_gemm2<256, FMT, TP>(d, p, mx, ma, a, st);
   }
   return DQ_ERR_ARG;
 }
@@ -870,8 +871,11 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
   DeviceInfo* d = nullptr;
   int rc = current_device(&d);
   if (rc != DQ_OK) return rc;
-  const Plan p = make_plan(fmt, M, N, K, d->sms, tp == nullptr, allow_twophase && tp == nullptr,
-                           tp == nullptr, max_split_ws, gated);
+  // the column-parallel path takes the two-phase plan only when its caller
+  // lends a workspace (the dq_tp_linear_*_ws entry points)
+  const Plan p = make_plan(fmt, M, N, K, d->sms, tp == nullptr,
+                           allow_twophase && (tp == nullptr || ws != nullptr), tp == nullptr,
+                           max_split_ws, gated);
   if (max_split_ws != SIZE_MAX && p.ws > max_split_ws) return DQ_ERR_SCRATCH_LIMIT;
   if (p.ws > 0 && (ws == nullptr || ws_bytes < p.ws || !aligned(ws, 16))) return DQ_ERR_WORKSPACE;
 
@@ -896,7 +900,7 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
     // itself, group by group under the MMAs (the ready counters after the
     // scratch start at zero); pair mode 4 runs the decode as its own launch
     // first.
-    const bool separate = g_override_pair.load() == 4;
+    const bool separate = tp == nullptr && g_override_pair.load() == 4;
     unsigned int* ready =
         reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(ws) + twophase_counter_offset(N, K));
     if (separate) {
@@ -950,6 +954,26 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
     g.tp_counter = nullptr;
     g.tp_rank = 0;
     g.tp_epoch = 0;
+    if (tp != nullptr) {
+      // every rank's y [M, N * world] at column N * rank, then the flags
+      g.n_out = tp->world;
+      g.ldy = static_cast<int>(N * tp->world);
+      g.col0 = static_cast<int>(N * tp->rank);
+      g.vec_ok = (N % 8 == 0);
+      for (int r = 0; r < tp->world; ++r) {
+        g.outs[r] = tp->y_ranks[r];
+        g.tp_flags[r] = tp->flag_ranks[r];
+        g.vec_ok = g.vec_ok && aligned(tp->y_ranks[r], 16);
+      }
+      g.tp_counter = tp->counter;
+      g.tp_rank = tp->rank;
+      g.tp_epoch = tp->epoch;
+      rc = fmt == kFmtNF4 ? launch_bf16_gemm2_bm<kFmtNF4, true>(d, p, mx2, ma, g, st)
+                          : launch_bf16_gemm2_bm<kFmtFP8, true>(d, p, mx2, ma, g, st);
+      if (rc != DQ_OK) return rc;
+      tp_wait_kernel<<<1, 32, 0, st>>>(tp->flag_ranks[tp->rank], tp->world, tp->epoch, kTpWaitNs);
+      return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
+    }
     if (separate) return launch_bf16_gemm2_bm<-1>(d, p, mx2, ma, g, st);
     return fmt == kFmtNF4 ? launch_bf16_gemm2_bm<kFmtNF4>(d, p, mx2, ma, g, st)
                           : launch_bf16_gemm2_bm<kFmtFP8>(d, p, mx2, ma, g, st);
@@ -1047,7 +1071,8 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
 static int tp_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8_t* w,
                    const float* absmax, float scale, const void* bias, int64_t N, int rank,
                    int world, void* const* y_ranks, unsigned int* const* flag_ranks,
-                   unsigned int* counter, unsigned int epoch, cudaStream_t st) {
+                   unsigned int* counter, unsigned int epoch, cudaStream_t st,
+                   void* ws = nullptr, size_t ws_bytes = 0) {
   if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world) return DQ_ERR_ARG;
   if (y_ranks == nullptr || flag_ranks == nullptr || counter == nullptr) return DQ_ERR_ARG;
   if (N <= 0 || (N % world) != 0) return DQ_ERR_SHAPE;
@@ -1058,7 +1083,7 @@ static int tp_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8_t* 
   if (!aligned(counter, 4)) return DQ_ERR_ALIGN;
   if (M == 0) return DQ_OK;
   TpOpts tp{rank, world, y_ranks, flag_ranks, counter, epoch};
-  return linear_impl(fmt, x, M, K, w, absmax, scale, bias, N / world, y_ranks[rank], nullptr, 0,
+  return linear_impl(fmt, x, M, K, w, absmax, scale, bias, N / world, y_ranks[rank], ws, ws_bytes,
                      st, &tp);
 }
 
@@ -1375,6 +1400,27 @@ int dq_tp_linear_fp8(const void* x, int64_t M, int64_t K, const uint8_t* w8_shar
                      dq_stream_t stream) {
   return tp_impl(kFmtFP8, x, M, K, w8_shard, nullptr, scale, bias_shard, N, rank, world, y_ranks,
                  flag_ranks, counter, epoch, static_cast<cudaStream_t>(stream));
+}
+
+int dq_tp_linear_nf4_ws(const void* x, int64_t M, int64_t K, const uint8_t* packed_shard,
+                        const float* absmax_shard, const void* bias_shard, int64_t N, int rank,
+                        int world, void* const* y_ranks, unsigned int* const* flag_ranks,
+                        unsigned int* counter, unsigned int epoch, void* workspace,
+                        size_t workspace_bytes, dq_stream_t stream) {
+  if (workspace == nullptr) return DQ_ERR_WORKSPACE;
+  return tp_impl(kFmtNF4, x, M, K, packed_shard, absmax_shard, 0.f, bias_shard, N, rank, world,
+                 y_ranks, flag_ranks, counter, epoch, static_cast<cudaStream_t>(stream), workspace,
+                 workspace_bytes);
+}
+
+int dq_tp_linear_fp8_ws(const void* x, int64_t M, int64_t K, const uint8_t* w8_shard, float scale,
+                        const void* bias_shard, int64_t N, int rank, int world, void* const* y_ranks,
+                        unsigned int* const* flag_ranks, unsigned int* counter, unsigned int epoch,
+                        void* workspace, size_t workspace_bytes, dq_stream_t stream) {
+  if (workspace == nullptr) return DQ_ERR_WORKSPACE;
+  return tp_impl(kFmtFP8, x, M, K, w8_shard, nullptr, scale, bias_shard, N, rank, world, y_ranks,
+                 flag_ranks, counter, epoch, static_cast<cudaStream_t>(stream), workspace,
+                 workspace_bytes);
 }
 
 int dq_qk_norm_rope(const void* img, int64_t ld_img, const void* txt, int64_t ld_txt, int B,

@@ -194,16 +194,22 @@ class _ColumnParallelBase(torch.nn.Module):
             raise ValueError(f"{m} tokens exceed the group's buffer ({self.group.max_tokens})")
         return x2, m
 
-    def _launch(self, fn, x2, m, weight_args):
+    def _launch(self, fn, x2, m, weight_args, fmt):
+        """One column-parallel call through the workspace-taking entry point:
+        from 1024 tokens each rank runs the two-phase plan (its shard decoded
+        once into the workspace inside the GEMM launch)."""
         g = self.group
         epoch, y_ranks, own = g.next_call()
         n = self.out_features
         # the shared buffer is [max_tokens, max_n]; this call uses its first m*n
         stream = ctypes.c_void_p(torch.cuda.current_stream(x2.device).cuda_stream)
+        ws_bytes = max(ops.workspace_size(m, self.n1 - self.n0, self.in_features, fmt), 256)
+        ws = ops.workspace(x2.device, ws_bytes)
         b = self.bias
         rc = fn(ctypes.c_void_p(x2.data_ptr()), m, self.in_features, *weight_args,
                 None if b is None else ctypes.c_void_p(b.data_ptr()), n, g.rank, g.world,
-                y_ranks, g._flag_ranks, g._counter, epoch, stream)
+                y_ranks, g._flag_ranks, g._counter, epoch, ctypes.c_void_p(ws.data_ptr()), ws_bytes,
+                stream)
         _check(fn.__name__ if hasattr(fn, "__name__") else "dq_tp_linear", rc)
         return g.output_view(own, m, n)
 
@@ -247,9 +253,9 @@ class ColumnParallelNf4Linear(_ColumnParallelBase):
 
     def _forward_fused(self, x2, m):
         lib = _lib.lib()
-        return self._launch(lib.dq_tp_linear_nf4, x2, m,
+        return self._launch(lib.dq_tp_linear_nf4_ws, x2, m,
                             (ctypes.c_void_p(self.weight_nf4.data_ptr()),
-                             ctypes.c_void_p(self.weight_absmax.data_ptr())))
+                             ctypes.c_void_p(self.weight_absmax.data_ptr())), _lib.DQ_FMT_NF4)
 
     def _forward_local(self, x2):
         return ops.nf4_linear(x2, self.weight_nf4, self.weight_absmax, self.n1 - self.n0, self.bias)
@@ -272,8 +278,9 @@ class ColumnParallelFp8Linear(_ColumnParallelBase):
 
     def _forward_fused(self, x2, m):
         lib = _lib.lib()
-        return self._launch(lib.dq_tp_linear_fp8, x2, m,
-                            (ctypes.c_void_p(self.weight_fp8.data_ptr()), ctypes.c_float(self.scale)))
+        return self._launch(lib.dq_tp_linear_fp8_ws, x2, m,
+                            (ctypes.c_void_p(self.weight_fp8.data_ptr()), ctypes.c_float(self.scale)),
+                            _lib.DQ_FMT_FP8)
 
     def _forward_local(self, x2):
         return ops.fp8_linear(x2, self.weight_fp8.view(torch.float8_e4m3fn), self.scale, self.bias)

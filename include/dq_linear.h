@@ -187,6 +187,23 @@ int dq_tp_linear_fp8(const void* x, int64_t M, int64_t K, const uint8_t* w8_shar
                      unsigned int* const* flag_ranks, unsigned int* counter, unsigned int epoch,
                      dq_stream_t stream);
 
+/* The column-parallel linears with a workspace (`dq_workspace_size(M,
+ * N / world, K, fmt)` bytes, 16-byte aligned; workspace_bytes must be at least
+ * what this rank's shard plan needs): from 1024 tokens each rank then runs the
+ * two-phase plan -- its shard's weight decoded once into the workspace by the
+ * GEMM launch itself -- whose epilogue stores into every rank's y as above;
+ * below that the fused kernels, as without a workspace.  Results are the same
+ * bits either way.  NULL workspace: DQ_ERR_WORKSPACE. */
+int dq_tp_linear_nf4_ws(const void* x, int64_t M, int64_t K, const uint8_t* packed_shard,
+                        const float* absmax_shard, const void* bias_shard, int64_t N, int rank,
+                        int world, void* const* y_ranks, unsigned int* const* flag_ranks,
+                        unsigned int* counter, unsigned int epoch, void* workspace,
+                        size_t workspace_bytes, dq_stream_t stream);
+int dq_tp_linear_fp8_ws(const void* x, int64_t M, int64_t K, const uint8_t* w8_shard, float scale,
+                        const void* bias_shard, int64_t N, int rank, int world, void* const* y_ranks,
+                        unsigned int* const* flag_ranks, unsigned int* counter, unsigned int epoch,
+                        void* workspace, size_t workspace_bytes, dq_stream_t stream);
+
 /* The linears with an activation fused into the epilogue: act = DQ_ACT_NONE or
  * DQ_ACT_GELU_TANH, y = bf16(gelu_tanh(bf16(x . W^T + bias))).  Replaces the
  * reference's up-projection followed by nnf_gelu(approximate = "tanh")
