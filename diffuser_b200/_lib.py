@@ -56,10 +56,27 @@ SIGNATURES = {
                                            ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p),
                                            ctypes.c_void_p, ctypes.c_uint, ctypes.c_void_p, _c_sz,
                                            ctypes.c_void_p]),
+    "dq_tp_linear_nf4_mc_ws": (ctypes.c_int, [ctypes.c_void_p, _c_i64, _c_i64, ctypes.c_void_p,
+                                              ctypes.c_void_p, ctypes.c_void_p, _c_i64, ctypes.c_int,
+                                              ctypes.c_int, ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p,
+                                              ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p, ctypes.c_uint,
+                                              ctypes.c_void_p, _c_sz, ctypes.c_void_p]),
+    "dq_tp_linear_fp8_mc_ws": (ctypes.c_int, [ctypes.c_void_p, _c_i64, _c_i64, ctypes.c_void_p,
+                                              ctypes.c_float, ctypes.c_void_p, _c_i64, ctypes.c_int,
+                                              ctypes.c_int, ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p,
+                                              ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p, ctypes.c_uint,
+                                              ctypes.c_void_p, _c_sz, ctypes.c_void_p]),
     "dq_qk_norm_rope": (ctypes.c_int, [ctypes.c_void_p, _c_i64, ctypes.c_void_p, _c_i64, ctypes.c_int,
                                        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                        ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p]),
+    "dq_qkv_norm_rope": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_void_p),
+                                        ctypes.POINTER(_c_i64), ctypes.POINTER(ctypes.c_void_p),
+                                        ctypes.POINTER(_c_i64), ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                        ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_void_p),
+                                        ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_int),
+                                        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float,
+                                        ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]),
     "dq_heads_to_tokens": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                           ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
                                           ctypes.c_void_p]),

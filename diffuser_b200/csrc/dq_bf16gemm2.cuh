@@ -324,10 +324,14 @@ __global__ void __launch_bounds__(Bf16PairCfg<BM, FMT>::kThreads, 1)
               const size_t off = static_cast<size_t>(m) * args.ldy + args.col0 + nc;
               if (args.vec_ok && nc + 8 <= args.N) {
                 const uint4 v16 = lds128(stg_s + 2u * (row * 32 + col));
+                if (TP && args.out_mc != nullptr) {
+                  multimem_st16(reinterpret_cast<__nv_bfloat16*>(args.out_mc) + off, v16);
+                } else {
 #pragma unroll
-                for (int d = 0; d < (TP ? kMaxRanks : 1); ++d)
-                  if (d < args.n_out)
-                    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.outs[d]) + off) = v16;
+                  for (int d = 0; d < (TP ? kMaxRanks : 1); ++d)
+                    if (d < args.n_out)
+                      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.outs[d]) + off) = v16;
+                }
               } else {
                 const __nv_bfloat16* src = sb + row * 32 + col;
 #pragma unroll

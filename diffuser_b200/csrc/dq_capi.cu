@@ -725,6 +725,7 @@ struct TpOpts {
   unsigned int* const* flag_ranks;
   unsigned int* counter;
   unsigned int epoch;
+  void* y_mc;  // multicast address of the call's y (all ranks' y buffers), or nullptr
 };
 
 static constexpr unsigned long long kTpWaitNs = 5000000000ull;  // 5 s
@@ -922,7 +923,7 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
         !make_map_2d(&ma, ws, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, N, K * 2, 64, 128,
                      CU_TENSOR_MAP_SWIZZLE_128B))
       return DQ_ERR_CUDA;
-    GemmArgs g;
+    GemmArgs g = {};
     g.absmax = static_cast<const float*>(absmax);
     g.scale_bf16 = sbf;
     g.bias = static_cast<const __nv_bfloat16*>(bias);
@@ -968,6 +969,7 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
       g.tp_counter = tp->counter;
       g.tp_rank = tp->rank;
       g.tp_epoch = tp->epoch;
+      g.out_mc = g.vec_ok && aligned(tp->y_mc, 16) ? tp->y_mc : nullptr;
       rc = fmt == kFmtNF4 ? launch_bf16_gemm2_bm<kFmtNF4, true>(d, p, mx2, ma, g, st)
                           : launch_bf16_gemm2_bm<kFmtFP8, true>(d, p, mx2, ma, g, st);
       if (rc != DQ_OK) return rc;
@@ -989,7 +991,7 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
                    fmt == kFmtNF4 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B))
     return DQ_ERR_CUDA;
 
-  GemmArgs a;
+  GemmArgs a = {};
   a.absmax = static_cast<const float*>(absmax);
   a.scale_bf16 = sbf;
   a.bias = static_cast<const __nv_bfloat16*>(bias);
@@ -1041,6 +1043,7 @@ static int linear_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8
     a.tp_counter = tp->counter;
     a.tp_rank = tp->rank;
     a.tp_epoch = tp->epoch;
+    a.out_mc = a.vec_ok && aligned(tp->y_mc, 16) ? tp->y_mc : nullptr;
   }
   if (tp != nullptr) {
     rc = fmt == kFmtNF4 ? dispatch_gemm<kFmtNF4, 1>(d, p, mx, mw, a, st)
@@ -1072,7 +1075,7 @@ static int tp_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8_t* 
                    const float* absmax, float scale, const void* bias, int64_t N, int rank,
                    int world, void* const* y_ranks, unsigned int* const* flag_ranks,
                    unsigned int* counter, unsigned int epoch, cudaStream_t st,
-                   void* ws = nullptr, size_t ws_bytes = 0) {
+                   void* ws = nullptr, size_t ws_bytes = 0, void* y_mc = nullptr) {
   if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world) return DQ_ERR_ARG;
   if (y_ranks == nullptr || flag_ranks == nullptr || counter == nullptr) return DQ_ERR_ARG;
   if (N <= 0 || (N % world) != 0) return DQ_ERR_SHAPE;
@@ -1082,7 +1085,7 @@ static int tp_impl(int fmt, const void* x, int64_t M, int64_t K, const uint8_t* 
   }
   if (!aligned(counter, 4)) return DQ_ERR_ALIGN;
   if (M == 0) return DQ_OK;
-  TpOpts tp{rank, world, y_ranks, flag_ranks, counter, epoch};
+  TpOpts tp{rank, world, y_ranks, flag_ranks, counter, epoch, y_mc};
   return linear_impl(fmt, x, M, K, w, absmax, scale, bias, N / world, y_ranks[rank], ws, ws_bytes,
                      st, &tp);
 }
@@ -1423,6 +1426,32 @@ int dq_tp_linear_fp8_ws(const void* x, int64_t M, int64_t K, const uint8_t* w8_s
                  workspace_bytes);
 }
 
+int dq_tp_linear_nf4_mc_ws(const void* x, int64_t M, int64_t K, const uint8_t* packed_shard,
+                           const float* absmax_shard, const void* bias_shard, int64_t N, int rank,
+                           int world, void* const* y_ranks, void* y_multicast,
+                           unsigned int* const* flag_ranks, unsigned int* counter,
+                           unsigned int epoch, void* workspace, size_t workspace_bytes,
+                           dq_stream_t stream) {
+  if (workspace == nullptr) return DQ_ERR_WORKSPACE;
+  if (y_multicast == nullptr) return DQ_ERR_ARG;
+  return tp_impl(kFmtNF4, x, M, K, packed_shard, absmax_shard, 0.f, bias_shard, N, rank, world,
+                 y_ranks, flag_ranks, counter, epoch, static_cast<cudaStream_t>(stream), workspace,
+                 workspace_bytes, y_multicast);
+}
+
+int dq_tp_linear_fp8_mc_ws(const void* x, int64_t M, int64_t K, const uint8_t* w8_shard,
+                           float scale, const void* bias_shard, int64_t N, int rank, int world,
+                           void* const* y_ranks, void* y_multicast,
+                           unsigned int* const* flag_ranks, unsigned int* counter,
+                           unsigned int epoch, void* workspace, size_t workspace_bytes,
+                           dq_stream_t stream) {
+  if (workspace == nullptr) return DQ_ERR_WORKSPACE;
+  if (y_multicast == nullptr) return DQ_ERR_ARG;
+  return tp_impl(kFmtFP8, x, M, K, w8_shard, nullptr, scale, bias_shard, N, rank, world, y_ranks,
+                 flag_ranks, counter, epoch, static_cast<cudaStream_t>(stream), workspace,
+                 workspace_bytes, y_multicast);
+}
+
 int dq_qk_norm_rope(const void* img, int64_t ld_img, const void* txt, int64_t ld_txt, int B,
                     int S_img, int S_txt, int H, int D, const void* w_img, const void* w_txt,
                     const float* cos_t, const float* sin_t, float eps, void* out,
@@ -1456,6 +1485,66 @@ int dq_qk_norm_rope(const void* img, int64_t ld_img, const void* txt, int64_t ld
     case 4: vec ? launch(qk_norm_rope_kernel<4, true>) : launch(qk_norm_rope_kernel<4, false>); break;
     case 6: vec ? launch(qk_norm_rope_kernel<6, true>) : launch(qk_norm_rope_kernel<6, false>); break;
     case 8: vec ? launch(qk_norm_rope_kernel<8, true>) : launch(qk_norm_rope_kernel<8, false>); break;
+    default:
+      return DQ_ERR_SHAPE;
+  }
+  return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
+}
+
+int dq_qkv_norm_rope(int nparts, const void* const* img, const int64_t* ld_img,
+                     const void* const* txt, const int64_t* ld_txt, int B, int S_img, int S_txt,
+                     int H, int D, const void* const* w_img, const void* const* w_txt,
+                     const int* rope, const float* cos_t, const float* sin_t, float eps,
+                     void* const* out, dq_stream_t stream) {
+  if (nparts < 1 || nparts > 3) return DQ_ERR_ARG;
+  if (B <= 0 || S_img < 0 || S_txt < 0 || H <= 0 || D <= 0 || D % 64 != 0 || D > 256)
+    return DQ_ERR_SHAPE;
+  if (img == nullptr || ld_img == nullptr || out == nullptr || w_img == nullptr || w_txt == nullptr ||
+      rope == nullptr || (S_txt > 0 && (txt == nullptr || ld_txt == nullptr)))
+    return DQ_ERR_ARG;
+  QkvParts parts = {};
+  parts.nparts = nparts;
+  bool vec = aligned(cos_t, 16) && aligned(sin_t, 16);
+  bool any_rope = false;
+  for (int p = 0; p < nparts; ++p) {
+    QkvPart& P = parts.p[p];
+    P.img = static_cast<const __nv_bfloat16*>(img[p]);
+    P.txt = S_txt > 0 ? static_cast<const __nv_bfloat16*>(txt[p]) : nullptr;
+    P.w_img = static_cast<const __nv_bfloat16*>(w_img[p]);
+    P.w_txt = static_cast<const __nv_bfloat16*>(w_txt[p]);
+    P.out = static_cast<__nv_bfloat16*>(out[p]);
+    P.ld_img = ld_img[p];
+    P.ld_txt = S_txt > 0 ? ld_txt[p] : 0;
+    P.rope = rope[p] != 0;
+    any_rope = any_rope || P.rope;
+    if (P.img == nullptr || P.out == nullptr || (S_txt > 0 && P.txt == nullptr)) return DQ_ERR_ARG;
+    // with text tokens both streams are normalized or neither
+    if (S_txt > 0 && (P.w_img == nullptr) != (P.w_txt == nullptr)) return DQ_ERR_ARG;
+    if (P.ld_img < static_cast<int64_t>(H) * D || (S_txt > 0 && P.ld_txt < static_cast<int64_t>(H) * D))
+      return DQ_ERR_SHAPE;
+    vec = vec && aligned(P.img, 16) && aligned(P.txt, 16) && aligned(P.out, 16) &&
+          aligned(P.w_img, 16) && aligned(P.w_txt, 16) && P.ld_img % 8 == 0 &&
+          (S_txt == 0 || P.ld_txt % 8 == 0);
+  }
+  if (any_rope && (cos_t == nullptr || sin_t == nullptr)) return DQ_ERR_ARG;
+  const int64_t items = static_cast<int64_t>(B) * (S_img + S_txt) * nparts *
+                        ((H + kHeadsPerWarp - 1) / kHeadsPerWarp);
+  if (items == 0) return DQ_OK;
+  DeviceInfo* d = nullptr;
+  const int rc = current_device(&d);
+  if (rc != DQ_OK) return rc;
+  // 8 warps per CTA, at most 8 CTAs per SM: the resident grid walks the items
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((items + 7) / 8,
+                                                                           static_cast<int64_t>(d->sms) * 8)));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto launch = [&](auto kern) {
+    kern<<<grid, 256, 0, st>>>(parts, B, S_img, S_txt, H, cos_t, sin_t, eps);
+  };
+  switch (D / 32) {
+    case 2: vec ? launch(qkv_norm_rope_kernel<2, true>) : launch(qkv_norm_rope_kernel<2, false>); break;
+    case 4: vec ? launch(qkv_norm_rope_kernel<4, true>) : launch(qkv_norm_rope_kernel<4, false>); break;
+    case 6: vec ? launch(qkv_norm_rope_kernel<6, true>) : launch(qkv_norm_rope_kernel<6, false>); break;
+    case 8: vec ? launch(qkv_norm_rope_kernel<8, true>) : launch(qkv_norm_rope_kernel<8, false>); break;
     default:
       return DQ_ERR_SHAPE;
   }
@@ -1534,6 +1623,13 @@ int dq_gated_residual(const void* x, int64_t ld_x, const void* gate, int64_t ld_
   const int rc = current_device(&d);
   if (rc != DQ_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (D % 8 == 0 && aligned(x, 16) && aligned(gate, 16) && aligned(y, 16) && aligned(out, 16) &&
+      ld_x % 8 == 0 && ld_mod % 8 == 0 && ld_y % 8 == 0 && ld_out % 8 == 0) {
+    gated_residual16_kernel<<<grid_for((T * (D / 8) + 1) / 2, 256, d->sms), 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(x), ld_x, static_cast<const __nv_bfloat16*>(gate), ld_mod,
+        static_cast<const __nv_bfloat16*>(y), ld_y, T, S, D, static_cast<__nv_bfloat16*>(out), ld_out);
+    return cudaGetLastError() == cudaSuccess ? DQ_OK : DQ_ERR_LAUNCH;
+  }
   gated_residual_kernel<<<grid_for(T * (D / 4), 256, d->sms), 256, 0, st>>>(
       static_cast<const __nv_bfloat16*>(x), ld_x, static_cast<const __nv_bfloat16*>(gate), ld_mod,
       static_cast<const __nv_bfloat16*>(y), ld_y, T, S, D, static_cast<__nv_bfloat16*>(out), ld_out);

@@ -171,6 +171,98 @@ __global__ void __launch_bounds__(512)
   }
 }
 
+// q, k and v of one attention in one launch.  Part p (0..nparts-1) reads its
+// image / text token rows from its own pointers (column views of the
+// concatenated q/k/v projection output or separate tensors), normalizes with
+// its own weights when it has them, rotates when `rope` is set, and writes its
+// own head-major [B, H, S_txt + S_img, D] output -- per part exactly the
+// arithmetic of qk_norm_rope_kernel, so the bits are the same.  Work items are
+// (token, part, group of HPW heads), taken by warps in a grid-stride loop:
+// every warp of the resident grid keeps its HPW head vectors (plus the
+// token's cos / sin slice) in flight, instead of the short-lived per-token
+// CTAs of the one-part kernel.
+struct QkvPart {
+  const __nv_bfloat16* img;
+  const __nv_bfloat16* txt;
+  const __nv_bfloat16* w_img;
+  const __nv_bfloat16* w_txt;
+  __nv_bfloat16* out;
+  int64_t ld_img, ld_txt;
+  int rope;
+};
+struct QkvParts {
+  QkvPart p[3];
+  int nparts;
+};
+
+template <int EPL, bool VEC>
+__global__ void __launch_bounds__(256)
+    qkv_norm_rope_kernel(const QkvParts parts, int B, int S_img, int S_txt, int H,
+                         const float* __restrict__ cos_t, const float* __restrict__ sin_t, float eps) {
+  constexpr int D = EPL * 32;
+  constexpr int HPW = kHeadsPerWarp;
+  const int lane = threadIdx.x & 31;
+  const int S = S_txt + S_img;
+  const int G = (H + HPW - 1) / HPW;
+  const int64_t per_token = static_cast<int64_t>(parts.nparts) * G;
+  const int64_t items = static_cast<int64_t>(B) * S * per_token;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t it = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items;
+       it += nwarps) {
+    const int64_t bs = it / per_token;  // b * S + s
+    const int rem = static_cast<int>(it - bs * per_token);
+    const int pi = rem / G;
+    const int h0 = (rem - pi * G) * HPW;
+    const int b = static_cast<int>(bs / S);
+    const int s = static_cast<int>(bs - static_cast<int64_t>(b) * S);
+    // select the part without indexing the parameter array dynamically
+    const QkvPart P = pi == 0 ? parts.p[0] : (pi == 1 ? parts.p[1] : parts.p[2]);
+    const bool is_txt = s < S_txt;
+    const __nv_bfloat16* row = is_txt ? P.txt + (static_cast<int64_t>(b) * S_txt + s) * P.ld_txt
+                                      : P.img + (static_cast<int64_t>(b) * S_img + (s - S_txt)) * P.ld_img;
+    const __nv_bfloat16* w = is_txt ? P.w_txt : P.w_img;
+    float x[HPW][EPL], wv[EPL], c[EPL], sn[EPL];
+#pragma unroll
+    for (int j = 0; j < HPW; ++j)
+      if (h0 + j < H) load_bf16_run<EPL, VEC>(row + static_cast<int64_t>(h0 + j) * D + EPL * lane, x[j]);
+    if (w != nullptr) load_bf16_run<EPL, VEC>(w + EPL * lane, wv);
+    if (P.rope) {
+      load_f32_run<EPL, VEC>(cos_t + static_cast<int64_t>(s) * D + EPL * lane, c);
+      load_f32_run<EPL, VEC>(sin_t + static_cast<int64_t>(s) * D + EPL * lane, sn);
+    }
+#pragma unroll
+    for (int j = 0; j < HPW; ++j) {
+      const int h = h0 + j;
+      if (h >= H) break;  // warp-uniform
+      if (w != nullptr) {
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) ss += x[j][i] * x[j][i];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float r = rsqrtf(ss / static_cast<float>(D) + eps);
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) {
+          const float n = __bfloat162float(__float2bfloat16_rn(x[j][i] * r));
+          x[j][i] = __bfloat162float(__float2bfloat16_rn(n * wv[i]));
+        }
+      }
+      __nv_bfloat16* dst = P.out + ((static_cast<int64_t>(b) * H + h) * S + s) * D + EPL * lane;
+      if (P.rope) {
+        float o[EPL];
+#pragma unroll
+        for (int i = 0; i < EPL; i += 2) {
+          o[i] = __fadd_rn(__fmul_rn(x[j][i], c[i]), __fmul_rn(-x[j][i + 1], sn[i]));
+          o[i + 1] = __fadd_rn(__fmul_rn(x[j][i + 1], c[i + 1]), __fmul_rn(x[j][i], sn[i + 1]));
+        }
+        store_bf16_run<EPL, VEC>(dst, o);
+      } else {
+        store_bf16_run<EPL, VEC>(dst, x[j]);
+      }
+    }
+  }
+}
+
 // One CTA per token, warps over groups of HPW heads (as above).
 template <int EPL, bool VEC>
 __global__ void __launch_bounds__(512)
@@ -291,6 +383,52 @@ __global__ void __launch_bounds__(256)
         y[e] = bf16r(n * bf16r(a[e] + 1.0f)) + c[e];
       }
       o[r] = pack_bf16x4(y);
+    }
+  }
+}
+
+// Gated residual with 16-byte accesses (rows, gate and output 16-byte
+// aligned, D a multiple of 8): each thread takes two 8-feature runs per
+// iteration, so four 16-byte loads are in flight per thread.
+__global__ void __launch_bounds__(256)
+    gated_residual16_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld_x,
+                            const __nv_bfloat16* __restrict__ gate, int64_t ld_mod,
+                            const __nv_bfloat16* __restrict__ y, int64_t ld_y, int64_t T, int S, int D,
+                            __nv_bfloat16* out, int64_t ld_out) {
+  const int nrun = D / 8;
+  const int64_t total = T * nrun;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i0 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i0 < total;
+       i0 += 2 * stride) {
+    uint4 xu[2], yu[2], gu[2];
+    int64_t tt[2];
+    int rr[2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int64_t i = i0 + q * stride;
+      tt[q] = i / nrun;
+      rr[q] = static_cast<int>(i - tt[q] * nrun);
+      if (i < total) {
+        const int b = static_cast<int>(tt[q] / S);
+        xu[q] = reinterpret_cast<const uint4*>(x + tt[q] * ld_x)[rr[q]];
+        yu[q] = reinterpret_cast<const uint4*>(y + tt[q] * ld_y)[rr[q]];
+        gu[q] = reinterpret_cast<const uint4*>(gate + b * ld_mod)[rr[q]];
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      if (i0 + q * stride >= total) break;
+      float xv[8], gv[8], yv[8], o[8];
+      unpack_bf16x4(make_uint2(xu[q].x, xu[q].y), xv);
+      unpack_bf16x4(make_uint2(xu[q].z, xu[q].w), xv + 4);
+      unpack_bf16x4(make_uint2(gu[q].x, gu[q].y), gv);
+      unpack_bf16x4(make_uint2(gu[q].z, gu[q].w), gv + 4);
+      unpack_bf16x4(make_uint2(yu[q].x, yu[q].y), yv);
+      unpack_bf16x4(make_uint2(yu[q].z, yu[q].w), yv + 4);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = xv[e] + bf16r(gv[e] * yv[e]);
+      const uint2 lo = pack_bf16x4(o), hi = pack_bf16x4(o + 4);
+      reinterpret_cast<uint4*>(out + tt[q] * ld_out)[rr[q]] = make_uint4(lo.x, lo.y, hi.x, hi.y);
     }
   }
 }

@@ -94,6 +94,10 @@ struct GemmArgs {
   // memory) in the column-parallel linear.
   void* outs[kMaxRanks];
   int n_out, ldy, col0;
+  // column-parallel through a multicast mapping: when out_mc != nullptr the
+  // 16-byte stores go once to out_mc[m * ldy + col0 + n] (multimem.st, all
+  // ranks' y at once) instead of to each outs[d]
+  void* out_mc;
   // Column-parallel completion: when tp_counter != nullptr every CTA fences
   // its stores system-wide and counts itself done; the last one raises flag
   // tp_rank of every rank's flag array (tp_flags[d]) to tp_epoch.
@@ -653,10 +657,14 @@ __global__ void __launch_bounds__(GemmCfg<FMT, BM>::kThreads, 1)
                 if (args.vec_ok && nc + 8 <= args.N) {
                   const uint4 v16 = lds128(stg_s + 2u * (row * 32 + col));
                   if constexpr (TP) {
+                    if (args.out_mc != nullptr) {
+                      multimem_st16(reinterpret_cast<__nv_bfloat16*>(args.out_mc) + off, v16);
+                    } else {
 #pragma unroll
-                    for (int d = 0; d < kMaxRanks; ++d)
-                      if (d < args.n_out)
-                        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.outs[d]) + off) = v16;
+                      for (int d = 0; d < kMaxRanks; ++d)
+                        if (d < args.n_out)
+                          *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.outs[d]) + off) = v16;
+                    }
                   } else {
                     *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.outs[0]) + off) = v16;
                   }

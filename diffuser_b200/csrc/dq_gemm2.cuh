@@ -446,10 +446,14 @@ __global__ void __launch_bounds__(Gemm2Cfg<FMT, BM>::kThreads, 1)
                 if (args.vec_ok && nc + 8 <= args.N) {
                   const uint4 v16 = lds128(stg_s + 2u * (row * 32 + col));
                   if constexpr (TP) {
+                    if (args.out_mc != nullptr) {
+                      multimem_st16(reinterpret_cast<__nv_bfloat16*>(args.out_mc) + off, v16);
+                    } else {
 #pragma unroll
-                    for (int d = 0; d < kMaxRanks; ++d)
-                      if (d < args.n_out)
-                        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.outs[d]) + off) = v16;
+                      for (int d = 0; d < kMaxRanks; ++d)
+                        if (d < args.n_out)
+                          *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.outs[d]) + off) = v16;
+                    }
                   } else {
                     *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.outs[0]) + off) = v16;
                   }

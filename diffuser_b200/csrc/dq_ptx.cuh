@@ -66,6 +66,16 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// One 16-byte store through an NVLink multicast address: the NVSwitch writes
+// it into every GPU whose memory is bound to the multicast object.  Relaxed,
+// system scope; the column-parallel completion (a system-wide fence, then
+// release stores of the ranks' flags) orders it like a plain peer store.
+__device__ __forceinline__ void multimem_st16(void* mc, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(v.x),
+               "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
 // Orders this thread's generic-proxy view of global memory against its
 // async-proxy (TMA) accesses: data that other threads wrote with ordinary
 // stores, acquired through a counter, is then seen by the TMA loads issued

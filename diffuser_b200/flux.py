@@ -55,6 +55,39 @@ def qk_norm_rope(img, txt, heads: int, w_img=None, w_txt=None, rope=None, eps: f
     return out
 
 
+def qkv_norm_rope(parts_img, parts_txt, heads: int, norms_img, norms_txt, ropes, rope=None,
+                  eps: float = 1e-6):
+    """qk_norm_rope for up to three tensors (q, k, v) of one attention in one
+    launch: part p reads parts_img[p] (and parts_txt[p]), normalizes with
+    norms_img[p] / norms_txt[p] when given, rotates when ropes[p] is set, and
+    returns its own [B, H, S_txt + S_img, D] tensor -- the same bits as one
+    qk_norm_rope call per part."""
+    n = len(parts_img)
+    b, s_img, hd = parts_img[0].shape
+    d = hd // heads
+    s_txt = 0 if parts_txt[0] is None else parts_txt[0].shape[1]
+    imgs = [t if t.stride(-1) == 1 else t.contiguous() for t in parts_img]
+    txts = [None if t is None else (t if t.stride(-1) == 1 else t.contiguous()) for t in parts_txt]
+    outs = [torch.empty((b, heads, s_txt + s_img, d), dtype=torch.bfloat16, device=imgs[0].device)
+            for _ in range(n)]
+    cos = sin = None
+    if rope is not None:
+        cos, sin = rope[0].contiguous(), rope[1].contiguous()
+    P = ctypes.c_void_p * n
+    L = ctypes.c_int64 * n
+    stream = ctypes.c_void_p(torch.cuda.current_stream(imgs[0].device).cuda_stream)
+    ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    rc = _lib.lib().dq_qkv_norm_rope(
+        n, P(*[ptr(t) for t in imgs]), L(*[t.stride(1) for t in imgs]),
+        P(*[ptr(t) for t in txts]) if s_txt else None,
+        L(*[0 if t is None else t.stride(1) for t in txts]) if s_txt else None,
+        b, s_img, s_txt, heads, d, P(*[ptr(w) for w in norms_img]), P(*[ptr(w) for w in norms_txt]),
+        (ctypes.c_int * n)(*[1 if r else 0 for r in ropes]), _ptr(cos), _ptr(sin), ctypes.c_float(eps),
+        P(*[t.data_ptr() for t in outs]), stream)
+    _lib.check("dq_qkv_norm_rope", rc)
+    return outs
+
+
 def heads_to_tokens(x, s_txt: int, img_out=None):
     """[B, H, S_txt + S_img, D] -> (txt [B, S_txt, H*D] or None, img [B, S_img, H*D]);
     img_out, if given, is a [B, S_img, H*D] view (e.g. the first columns of a
@@ -395,9 +428,14 @@ class FluxAttention(nn.Module):
                                       self.add_k_proj, self.add_v_proj)
             wq_t, wk_t = self.norm_added_q.weight, self.norm_added_k.weight
         q_i, k_i, v_i = self._qkv(x, getattr(self, "to_qkv", None), self.to_q, self.to_k, self.to_v)
-        q = qk_norm_rope(q_i, q_t, h, self.norm_q.weight, wq_t, rope, self.norm_q.eps)
-        k = qk_norm_rope(k_i, k_t, h, self.norm_k.weight, wk_t, rope, self.norm_k.eps)
-        v = qk_norm_rope(v_i, v_t, h)
+        if self.norm_q.eps == self.norm_k.eps:
+            q, k, v = qkv_norm_rope((q_i, k_i, v_i), (q_t, k_t, v_t), h,
+                                    (self.norm_q.weight, self.norm_k.weight, None), (wq_t, wk_t, None),
+                                    (rope is not None, rope is not None, False), rope, self.norm_q.eps)
+        else:
+            q = qk_norm_rope(q_i, q_t, h, self.norm_q.weight, wq_t, rope, self.norm_q.eps)
+            k = qk_norm_rope(k_i, k_t, h, self.norm_k.weight, wk_t, rope, self.norm_k.eps)
+            v = qk_norm_rope(v_i, v_t, h)
         att = F.scaled_dot_product_attention(q, k, v, dropout_p=0.0, is_causal=False)
         txt_len = 0 if ctx is None else ctx.shape[1]
         # `out` (pre-only attention): the image tokens go straight there

@@ -10,9 +10,12 @@ buffer is the contiguous byte range [n0*K/2, n1*K/2) and of absmax the range
 `forward` runs the fused dequant-GEMM on the local shard and its epilogue
 stores every output tile straight into every rank's y [M, N] over NVLink
 (peer pointers from CUDA IPC), then raises a per-rank flag; a bounded device
-wait completes the call.  There is no library collective on this path;
-`forward_nccl` is the conventional alternative (local GEMM, NCCL all-gather,
-column permute) kept for comparison.
+wait completes the call.  With `TpGroup(..., multicast=True)` the y buffers
+are symmetric memory bound to an NVLink multicast object and each epilogue
+store is a single `multimem.st` that the NVSwitch writes into every rank's y:
+a rank's NVLink egress is its own block once instead of once per peer.  There
+is no library collective on this path; `forward_nccl` is the conventional
+alternative (local GEMM, NCCL all-gather, column permute) kept for comparison.
 
 Every rank must call the same modules in the same order with the same token
 count.  The returned y is a view of a shared buffer that is double-buffered:
@@ -89,7 +92,8 @@ class TpGroup:
     (gloo is enough: it only carries the 64-byte IPC handles once).
     """
 
-    def __init__(self, max_tokens: int, max_out_features: int, pg=None, device=None):
+    def __init__(self, max_tokens: int, max_out_features: int, pg=None, device=None,
+                 multicast: bool = False):
         import torch.distributed as dist
         self.pg = pg
         self.rank = dist.get_rank(pg)
@@ -104,22 +108,29 @@ class TpGroup:
         lib = _lib.lib()
         ybytes = self.max_tokens * self.max_n * 2
         self._own = []
+        self._symm = None
+        self._mc = None
         with torch.cuda.device(self.device):
-            for nbytes in (ybytes, ybytes, 256, 256):  # y0, y1, flags, counter
+            if multicast:
+                ys = self._symmetric_y(ybytes)
+                shared = (256,)  # flags (the counter below is never shared)
+            else:
+                shared = (ybytes, ybytes, 256)  # y0, y1, flags
+            for nbytes in shared + (256,):  # ..., counter
                 p = ctypes.c_void_p()
                 _check("dq_tp_buffer_alloc", lib.dq_tp_buffer_alloc(nbytes, ctypes.byref(p)))
                 self._own.append(p.value)
             handles = []
-            for p in self._own[:3]:
+            for p in self._own[:len(shared)]:
                 h = ctypes.create_string_buffer(_lib.DQ_IPC_HANDLE_BYTES)
                 _check("dq_ipc_handle", lib.dq_ipc_handle(ctypes.c_void_p(p), h))
                 handles.append(h.raw)
             gathered = [None] * self.world
             dist.all_gather_object(gathered, handles, group=pg)
             self._opened = []
-            ptrs = [[None] * self.world for _ in range(3)]
+            ptrs = [[None] * self.world for _ in range(len(shared))]
             for q in range(self.world):
-                for j in range(3):
+                for j in range(len(shared)):
                     if q == self.rank:
                         ptrs[j][q] = self._own[j]
                     else:
@@ -127,17 +138,46 @@ class TpGroup:
                         _check("dq_ipc_open", lib.dq_ipc_open(gathered[q][j], ctypes.byref(p)))
                         self._opened.append(p.value)
                         ptrs[j][q] = p.value
+        if multicast:
+            ptrs = ys + ptrs
         arr = ctypes.c_void_p * self.world
         self._y_ranks = [arr(*ptrs[0]), arr(*ptrs[1])]
         self._flag_ranks = arr(*ptrs[2])
-        self._counter = ctypes.c_void_p(self._own[3])
+        self._counter = ctypes.c_void_p(self._own[-1])
         self._closed = False
 
+    @property
+    def multicast(self) -> bool:
+        return self._mc is not None
+
+    def _symmetric_y(self, ybytes: int):
+        """The two y buffers as one symmetric-memory allocation bound to an
+        NVLink multicast object.  Returns the per-rank pointer lists of both
+        halves and keeps the multicast address of each half."""
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+        group = self.pg if self.pg is not None else dist.group.WORLD
+        try:  # older releases need the group registered first
+            symm.enable_symm_mem_for_group(group.group_name)
+        except Exception:  # noqa: BLE001 - newer ones need nothing
+            pass
+        buf = symm.empty(2 * ybytes // 2, dtype=torch.bfloat16, device=self.device)
+        hdl = symm.rendezvous(buf, group)
+        base = buf.data_ptr()
+        peers = list(hdl.buffer_ptrs)
+        if not hdl.multicast_ptr or peers[self.rank] != base:
+            raise RuntimeError("NVLink multicast is not available for this group")
+        self._symm = (buf, hdl)
+        self._mc = [hdl.multicast_ptr, hdl.multicast_ptr + ybytes]
+        return [[p for p in peers], [p + ybytes for p in peers]]
+
     def next_call(self):
-        """Advance to the next call: (epoch, y-rank pointer array, own y ptr)."""
+        """Advance to the next call: (epoch, y-rank pointer array, own y ptr,
+        multicast address of the y buffer or None)."""
         self.epoch += 1
         buf = self.epoch & 1
-        return self.epoch, self._y_ranks[buf], self._own[buf]
+        own = self._y_ranks[buf][self.rank]
+        return self.epoch, self._y_ranks[buf], own, None if self._mc is None else self._mc[buf]
 
     def output_view(self, ptr: int, m: int, n: int) -> torch.Tensor:
         t = torch.as_tensor(_CudaView(ptr, (m, n), "<u2"), device=self.device)
@@ -158,6 +198,8 @@ class TpGroup:
             dist.barrier(group=self.pg)
             for p in self._own:
                 lib.dq_tp_buffer_free(ctypes.c_void_p(p))
+        self._symm = None
+        self._mc = None
         self._closed = True
 
 
@@ -199,17 +241,17 @@ class _ColumnParallelBase(torch.nn.Module):
         from 1024 tokens each rank runs the two-phase plan (its shard decoded
         once into the workspace inside the GEMM launch)."""
         g = self.group
-        epoch, y_ranks, own = g.next_call()
+        epoch, y_ranks, own, mc = g.next_call()
         n = self.out_features
         # the shared buffer is [max_tokens, max_n]; this call uses its first m*n
         stream = ctypes.c_void_p(torch.cuda.current_stream(x2.device).cuda_stream)
         ws_bytes = max(ops.workspace_size(m, self.n1 - self.n0, self.in_features, fmt), 256)
         ws = ops.workspace(x2.device, ws_bytes)
         b = self.bias
-        rc = fn(ctypes.c_void_p(x2.data_ptr()), m, self.in_features, *weight_args,
-                None if b is None else ctypes.c_void_p(b.data_ptr()), n, g.rank, g.world,
-                y_ranks, g._flag_ranks, g._counter, epoch, ctypes.c_void_p(ws.data_ptr()), ws_bytes,
-                stream)
+        head = (ctypes.c_void_p(x2.data_ptr()), m, self.in_features, *weight_args,
+                None if b is None else ctypes.c_void_p(b.data_ptr()), n, g.rank, g.world, y_ranks)
+        tail = (g._flag_ranks, g._counter, epoch, ctypes.c_void_p(ws.data_ptr()), ws_bytes, stream)
+        rc = fn(*head, *tail) if mc is None else fn(*head, ctypes.c_void_p(mc), *tail)
         _check(fn.__name__ if hasattr(fn, "__name__") else "dq_tp_linear", rc)
         return g.output_view(own, m, n)
 
@@ -253,7 +295,8 @@ class ColumnParallelNf4Linear(_ColumnParallelBase):
 
     def _forward_fused(self, x2, m):
         lib = _lib.lib()
-        return self._launch(lib.dq_tp_linear_nf4_ws, x2, m,
+        fn = lib.dq_tp_linear_nf4_mc_ws if self.group.multicast else lib.dq_tp_linear_nf4_ws
+        return self._launch(fn, x2, m,
                             (ctypes.c_void_p(self.weight_nf4.data_ptr()),
                              ctypes.c_void_p(self.weight_absmax.data_ptr())), _lib.DQ_FMT_NF4)
 
@@ -278,7 +321,8 @@ class ColumnParallelFp8Linear(_ColumnParallelBase):
 
     def _forward_fused(self, x2, m):
         lib = _lib.lib()
-        return self._launch(lib.dq_tp_linear_fp8_ws, x2, m,
+        fn = lib.dq_tp_linear_fp8_mc_ws if self.group.multicast else lib.dq_tp_linear_fp8_ws
+        return self._launch(fn, x2, m,
                             (ctypes.c_void_p(self.weight_fp8.data_ptr()), ctypes.c_float(self.scale)),
                             _lib.DQ_FMT_FP8)
 

@@ -28,6 +28,18 @@ int dq_qk_norm_rope(const void* img, int64_t ld_img, const void* txt, int64_t ld
                     const float* cos_t, const float* sin_t, float eps, void* out,
                     dq_stream_t stream);
 
+/* The q, k and v of one attention in one launch: part p (p < nparts <= 3)
+ * reads img[p] [B, S_img, H*D] (row stride ld_img[p]) and, if S_txt > 0,
+ * txt[p] [B, S_txt, H*D] (row stride ld_txt[p]), normalizes with
+ * w_img[p] / w_txt[p] when w_img[p] != NULL, rotates with cos_t / sin_t when
+ * rope[p] != 0, and writes out[p] [B, H, S_txt + S_img, D] -- the same bits as
+ * one dq_qk_norm_rope call per part.  The pointer arrays are host arrays. */
+int dq_qkv_norm_rope(int nparts, const void* const* img, const int64_t* ld_img,
+                     const void* const* txt, const int64_t* ld_txt, int B, int S_img, int S_txt,
+                     int H, int D, const void* const* w_img, const void* const* w_txt,
+                     const int* rope, const float* cos_t, const float* sin_t, float eps,
+                     void* const* out, dq_stream_t stream);
+
 /* in [B, H, S_txt + S_img, D] -> out_txt [B, S_txt, H*D] (if S_txt > 0) and
  * out_img [B, S_img, H*D]. */
 int dq_heads_to_tokens(const void* in, int B, int H, int S_txt, int S_img, int D, void* out_txt,

@@ -204,6 +204,28 @@ int dq_tp_linear_fp8_ws(const void* x, int64_t M, int64_t K, const uint8_t* w8_s
                         unsigned int* const* flag_ranks, unsigned int* counter, unsigned int epoch,
                         void* workspace, size_t workspace_bytes, dq_stream_t stream);
 
+/* The column-parallel linears with a workspace, writing through an NVLink
+ * multicast mapping: y_multicast is the multicast address of this call's y
+ * buffer (the same offset in every rank's y, as a symmetric-memory multicast
+ * object bound to all ranks' y buffers provides), so every 16-byte epilogue
+ * store is one `multimem.st` that the NVSwitch replicates into all ranks' y
+ * instead of one store per rank.  y_ranks stay required (unicast pointers for
+ * stores that are not 16-byte aligned and for nothing else); flags, counter,
+ * epoch and the bounded wait are as above.  The same bits as
+ * dq_tp_linear_*_ws.  NULL y_multicast: DQ_ERR_ARG. */
+int dq_tp_linear_nf4_mc_ws(const void* x, int64_t M, int64_t K, const uint8_t* packed_shard,
+                           const float* absmax_shard, const void* bias_shard, int64_t N, int rank,
+                           int world, void* const* y_ranks, void* y_multicast,
+                           unsigned int* const* flag_ranks, unsigned int* counter,
+                           unsigned int epoch, void* workspace, size_t workspace_bytes,
+                           dq_stream_t stream);
+int dq_tp_linear_fp8_mc_ws(const void* x, int64_t M, int64_t K, const uint8_t* w8_shard,
+                           float scale, const void* bias_shard, int64_t N, int rank, int world,
+                           void* const* y_ranks, void* y_multicast,
+                           unsigned int* const* flag_ranks, unsigned int* counter,
+                           unsigned int epoch, void* workspace, size_t workspace_bytes,
+                           dq_stream_t stream);
+
 /* The linears with an activation fused into the epilogue: act = DQ_ACT_NONE or
  * DQ_ACT_GELU_TANH, y = bf16(gelu_tanh(bf16(x . W^T + bias))).  Replaces the
  * reference's up-projection followed by nnf_gelu(approximate = "tanh")

@@ -115,6 +115,17 @@ def test_strided_and_glue_entry_points_reject_bad_arguments_on_host(lib):
                                  None) == 1
     assert lib.dq_adaln_modulate(p, 8, 5, 2, 8, p, p, 8, ctypes.c_float(1e-6), p, 8, None) == 1
     assert lib.dq_adaln_modulate(p, 8, 4, 2, 8, None, p, 8, ctypes.c_float(1e-6), p, 8, None) == 7
+    # q/k/v glue: no parts, a part with a row stride below H * D, rope without a table
+    P3 = ctypes.c_void_p * 3
+    L3 = ctypes.c_int64 * 3
+    I3 = ctypes.c_int * 3
+    ptrs, nul = P3(p, p, p), P3(None, None, None)
+    assert lib.dq_qkv_norm_rope(0, ptrs, L3(384, 384, 384), None, None, 1, 4, 0, 3, 128, nul, nul,
+                                I3(0, 0, 0), None, None, ctypes.c_float(1e-6), ptrs, None) == 7
+    assert lib.dq_qkv_norm_rope(3, ptrs, L3(384, 100, 384), None, None, 1, 4, 0, 3, 128, nul, nul,
+                                I3(0, 0, 0), None, None, ctypes.c_float(1e-6), ptrs, None) == 1
+    assert lib.dq_qkv_norm_rope(3, ptrs, L3(384, 384, 384), None, None, 1, 4, 0, 3, 128, nul, nul,
+                                I3(1, 0, 0), None, None, ctypes.c_float(1e-6), ptrs, None) == 7
     # gated residual: row stride below D, misaligned rows
     assert lib.dq_gated_residual(p, 4, p, 8, p, 8, 4, 2, 8, p, 8, None) == 1
     assert lib.dq_gated_residual(ctypes.c_void_p(0x1002), 8, p, 8, p, 8, 4, 2, 8, p, 8, None) == 2

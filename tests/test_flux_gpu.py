@@ -154,6 +154,41 @@ def test_fused_attention_glue_wide_and_scalar_accesses_agree():
             assert torch.equal(i_w, i_out) and (wide[..., H * D:] == 3.0).all()
 
 
+def test_qkv_glue_in_one_launch_matches_one_call_per_part():
+    # dq_qkv_norm_rope (q, k, v of one attention in one launch) gives the bits
+    # of three dq_qk_norm_rope calls: column views of one concatenated
+    # projection (aligned and unaligned rows), with and without text tokens
+    from diffuser_b200 import flux
+    torch.manual_seed(3)
+    dev = torch.device("cuda", 0)
+    for (B, S_img, S_txt, H, D, off) in ((2, 37, 9, 24, 128, 0), (1, 64, 0, 3, 64, 0),
+                                         (1, 5, 3, 2, 256, 0), (1, 11, 4, 5, 128, 1)):
+        hd = H * D
+        qkv_i = torch.randn(B, S_img, 3 * hd + off, device=dev).to(torch.bfloat16)[..., off:]
+        qkv_t = torch.randn(B, S_txt, 3 * hd + off, device=dev).to(torch.bfloat16)[..., off:] \
+            if S_txt else None
+        parts_i = [qkv_i[..., j * hd:(j + 1) * hd] for j in range(3)]
+        parts_t = [None if qkv_t is None else qkv_t[..., j * hd:(j + 1) * hd] for j in range(3)]
+        wq_i, wk_i, wq_t, wk_t = [(1 + 0.1 * torch.randn(D, device=dev)).to(torch.bfloat16)
+                                  for _ in range(4)]
+        if not S_txt:
+            wq_t = wk_t = None
+        pos = torch.randint(0, 64, (S_txt + S_img, 3), device=dev).float()
+        axes = {64: (16, 24, 24), 128: (16, 56, 56), 256: (32, 112, 112)}[D]
+        rope = flux.pos_embed(pos, axes)
+        with torch.no_grad():
+            q, k, v = flux.qkv_norm_rope(parts_i, parts_t, H, (wq_i, wk_i, None), (wq_t, wk_t, None),
+                                         (True, True, False), rope, 1e-6)
+            assert torch.equal(q, flux.qk_norm_rope(parts_i[0], parts_t[0], H, wq_i, wq_t, rope))
+            assert torch.equal(k, flux.qk_norm_rope(parts_i[1], parts_t[1], H, wk_i, wk_t, rope))
+            assert torch.equal(v, flux.qk_norm_rope(parts_i[2], parts_t[2], H))
+            # two parts, no rotary table
+            q2, v2 = flux.qkv_norm_rope(parts_i[0::2], parts_t[0::2], H, (wq_i, None), (wq_t, None),
+                                        (False, False), None, 1e-6)
+            assert torch.equal(q2, flux.qk_norm_rope(parts_i[0], parts_t[0], H, wq_i, wq_t))
+            assert torch.equal(v2, v)
+
+
 def test_adaln_glue_matches_tensor_ops():
     # AdaLN modulation and gated residual kernels vs the blocks' tensor-op
     # chains (R/dit_flux_modules.R:26-42, 54-70, 280-321): the residual is
@@ -162,7 +197,9 @@ def test_adaln_glue_matches_tensor_ops():
     from diffuser_b200 import flux
     torch.manual_seed(2)
     dev = torch.device("cuda", 0)
-    for (B, S, D) in ((2, 37, 256), (1, 65, 3072), (3, 5, 1028), (1, 3, 8192)):
+    # the residual uses 16-byte runs when rows allow
+    for (B, S, D) in ((2, 37, 256), (1, 65, 3072), (3, 5, 1028), (1, 3, 8192), (2, 9, 4096),
+                      (1, 7, 1000)):
         x = (torch.randn(B, S, D, device=dev) * 3 + 0.5).to(torch.bfloat16)
         mods = (torch.randn(B, 6 * D, device=dev) * 0.5).to(torch.bfloat16)
         p = mods.chunk(6, dim=1)                                  # strided [B, D] views

@@ -1,8 +1,11 @@
 """Column-parallel fused linear on 2..8 GPUs of one node (skipped with fewer
 than two): each rank's kernel writes its [M, N/world] block into every rank's
-y through CUDA-IPC peer pointers and a bounded flag barrier completes the
-call.  The assembled y must equal, bit for bit, the single-GPU fused linear
-on the full weight (split-K off on both sides), and the NCCL all-gather path."""
+y -- through CUDA-IPC peer pointers, or with one multimem store per 16 bytes
+through an NVLink multicast mapping of symmetric-memory y buffers -- and a
+bounded flag barrier completes the call.  The assembled y must equal, bit for
+bit, the single-GPU fused linear on the full weight (split-K off on both
+sides), and the NCCL all-gather path.  The failure test stays on the IPC path
+(no multicast object exists while a rank is made to miss a call)."""
 import datetime
 import os
 import socket
@@ -24,7 +27,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, out_dir):
+def _rank_main(rank, world, port, out_dir, multicast=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", rank=rank, world_size=world,
@@ -32,7 +35,17 @@ def _rank_main(rank, world, port, out_dir):
     nccl = dist.new_group(backend="nccl", timeout=datetime.timedelta(seconds=60))
     from diffuser_b200 import ops, tp
     results = []
-    grp = tp.TpGroup(max_tokens=2304, max_out_features=3072)
+    try:
+        grp = tp.TpGroup(max_tokens=2304, max_out_features=3072, pg=nccl if multicast else None,
+                         multicast=multicast)
+    except RuntimeError as e:
+        if "multicast" not in str(e):
+            raise
+        np.save(os.path.join(out_dir, f"tp_{rank}.npy"),
+                np.array([("no_multicast", 0, 0, 0, True, True, 0.0)], dtype=object), allow_pickle=True)
+        dist.destroy_process_group(nccl)
+        dist.destroy_process_group()
+        return
     try:
         for fmt in ("nf4", "fp8"):
             for (m, n, k) in SHAPES:
@@ -78,14 +91,17 @@ def _rank_main(rank, world, port, out_dir):
     np.save(os.path.join(out_dir, f"tp_{rank}.npy"), np.array(results, dtype=object), allow_pickle=True)
 
 
-def test_column_parallel_matches_single_gpu(tmp_path):
+@pytest.mark.parametrize("multicast", [False, True], ids=["peer_stores", "multimem"])
+def test_column_parallel_matches_single_gpu(tmp_path, multicast):
     world = min(torch.cuda.device_count(), 8)
     if world < 2:
         pytest.skip("needs at least two GPUs")
-    mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+    mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path), multicast), nprocs=world,
                        join=True, start_method="spawn")
     table = {r: [tuple(row) for row in np.load(tmp_path / f"tp_{r}.npy", allow_pickle=True)]
              for r in range(world)}
+    if any(row[0] == "no_multicast" for rows in table.values() for row in rows):
+        pytest.skip("NVLink multicast is not available on these GPUs")
     for r, rows in table.items():
         for fmt, m, n, k, fused_equal, nccl_equal, rel in rows:
             if fmt == "device_error":
