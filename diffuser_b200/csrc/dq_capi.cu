@@ -201,6 +201,7 @@ struct DeviceInfo {
   int bf16_max_pairs[2][3][6] = {};
   std::atomic<int> smallm_set[3][2][3];    // small-M kernel, [fmt, or 2 = NF4 with bf16 scales][token tiles - 1][row groups 1/2/4]
   std::atomic<int> smallm2_set[2][2][3];   // small-M TMA-ring kernel, [fmt][CTAs per SM - 2][row groups]
+  std::atomic<int> smallm2_mt2_set[2];     // ... with two token tiles, [fmt]
 };
 
 constexpr int kMaxDevices = 64;
@@ -339,14 +340,18 @@ static void smallm2_config(int64_t N, int sms, bool gated, int* r16_out, int* cp
       }
     }
 }
-// The TMA-ring kernel serves one 8-token tile and takes NF4 block-scale tiles
-// by TMA (rows of K / 64 floats must be whole 16-byte units).  Automatic up to
-// four tokens: from about eight, every consumer lane reads x through an L1
-// that the ring's shared memory has mostly taken, and the register-stream
-// kernel is faster (3072 -> 18432 at M = 8: 16.9 against 13.6 us).
+// The TMA-ring kernel takes NF4 block-scale tiles by TMA (rows of K / 64
+// floats must be whole 16-byte units).  One 8-token tile: automatic up to four
+// tokens (from about eight, every consumer lane reads x through an L1 that the
+// ring's shared memory has mostly taken, and the register-stream kernel is
+// faster: 3072 -> 18432 at M = 8, 16.7 against 13.9 us).  Two token tiles
+// (9-16 tokens, x staged in the ring, 64-row CTAs two per SM): automatic when
+// the grid fills at least 5/8 of those slots (measured, NF4 / fp8 at M = 16:
+// 3072 -> 18432 18.4 / 16.9 us against 20.9 / 18.0, 4096 -> 12288 23.3 / 20.6
+// against 25.6 / 20.6; 3072 -> 9216, one CTA per SM, 17.3 against 11.5).
 constexpr int64_t kSmallM2AutoMaxM = 4;
 static bool smallm2_shape_ok(int fmt, int64_t M, int64_t K) {
-  return M <= 8 && (fmt == kFmtNF4 ? K % 256 == 0 : K % 128 == 0);
+  return M <= 16 && (fmt == kFmtNF4 ? K % 256 == 0 : K % 128 == 0);
 }
 
 // Row groups per CTA of the register-stream small-M kernel; a gated
@@ -396,11 +401,20 @@ static Plan make_plan(int fmt, int64_t M, int64_t N, int64_t K, int sms, bool al
        (opair == 0 && obm == 0 && g_override_splits.load() == 0 &&
         (M <= 8 || smallm_r16(fmt, M, N, sms) >= 2)))) {
     p.smallm = true;
-    p.ring = smallm2_shape_ok(fmt, M, K) && (opair == 5 || (opair == 0 && M <= kSmallM2AutoMaxM));
+    p.ring = smallm2_shape_ok(fmt, M, K) &&
+             (opair == 5 || (opair == 0 && (M <= kSmallM2AutoMaxM ||
+                                            (M > 8 && (N + 63) / 64 >= (5 * static_cast<int64_t>(sms)) / 4))));
     p.bm = M <= 8 ? 8 : 16;
     p.m_tiles = 1;
     int r16 = smallm_rows(fmt, M, N, sms, gated);
-    if (p.ring) smallm2_config(N, sms, gated, &r16, &p.cps);
+    if (p.ring) {
+      if (M > 8) {  // two token tiles: x staged in the ring, 64-row CTAs, two per SM
+        r16 = 4;
+        p.cps = 2;
+      } else {
+        smallm2_config(N, sms, gated, &r16, &p.cps);
+      }
+    }
     p.r16 = r16;
     p.n_tiles = static_cast<int>((N + 16 * r16 - 1) / (16 * r16));
     p.tiles = p.n_tiles;
@@ -779,13 +793,15 @@ static int launch_smallm(DeviceInfo* d, const Plan& p, const void* x, const uint
 
 // The TMA-ring small-M kernel: one CTA per 16 * R16 weight rows, one 8-token
 // tile, CPS CTAs per SM.
-template <int FMT, int R16, int CPS>
+template <int FMT, int R16, int CPS, int MT = 1>
 static int launch_smallm2_cfg(DeviceInfo* d, const void* x, const uint8_t* w, const void* absmax,
                               float scale, const void* bias, void* y, int64_t M, int64_t N,
                               int64_t K, int act, int64_t ldy, cudaStream_t st) {
-  using C = SmallM2Cfg<FMT, 1, R16, CPS>;
-  auto kern = smallm2_kernel<FMT, 1, R16, CPS>;
-  const int rc = once_per_device(d->smallm2_set[FMT][CPS - 2][R16 == 4 ? 2 : R16 - 1], [&] {
+  using C = SmallM2Cfg<FMT, MT, R16, CPS>;
+  auto kern = smallm2_kernel<FMT, MT, R16, CPS>;
+  std::atomic<int>& set_flag = MT == 2 ? d->smallm2_mt2_set[FMT]
+                                       : d->smallm2_set[FMT][CPS - 2][R16 == 4 ? 2 : R16 - 1];
+  const int rc = once_per_device(set_flag, [&] {
     return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) ==
                    cudaSuccess
                ? static_cast<int>(DQ_OK)
@@ -804,6 +820,12 @@ static int launch_smallm2_cfg(DeviceInfo* d, const void* x, const uint8_t* w, co
   } else {
     ma = mw;  // unused
   }
+  CUtensorMap mx = mw;  // unused with one token tile
+  if constexpr (MT == 2) {
+    if (!make_map_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, M, K * 2, 64, 16,
+                     CU_TENSOR_MAP_SWIZZLE_128B))
+      return DQ_ERR_CUDA;
+  }
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -814,7 +836,7 @@ static int launch_smallm2_cfg(DeviceInfo* d, const void* x, const uint8_t* w, co
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kern, mw, ma, static_cast<const __nv_bfloat16*>(x), scale,
+  if (cudaLaunchKernelEx(&cfg, kern, mw, ma, mx, static_cast<const __nv_bfloat16*>(x), scale,
                          static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y),
                          static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), act,
                          ldy) != cudaSuccess)
@@ -837,6 +859,8 @@ template <int FMT>
 static int launch_smallm2(DeviceInfo* d, const Plan& p, const void* x, const uint8_t* w,
                           const void* absmax, float scale, const void* bias, void* y, int64_t M,
                           int64_t N, int64_t K, int act, int64_t ldy, cudaStream_t st) {
+  if (M > 8)
+    return launch_smallm2_cfg<FMT, 4, 2, 2>(d, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
   return p.cps == 3 ? launch_smallm2_r<FMT, 3>(d, p.r16, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st)
                     : launch_smallm2_r<FMT, 2>(d, p.r16, x, w, absmax, scale, bias, y, M, N, K, act, ldy, st);
 }

@@ -39,7 +39,13 @@
 // read of x, so only the weight and its scales are read early: they must not
 // be outputs of the immediately preceding decode-sized linear call.
 //
-// Requirements: at most 8 tokens, K % 128 == 0 (fp8) / K % 256 == 0 with
+// Two token tiles (9-16 tokens): x is staged with the weights -- per stage,
+// 16-row x 64-k TMA boxes of x (128-byte swizzle, rows past M zero-filled),
+// read by the consumers from shared memory instead of through L1 -- in 64-row
+// CTAs, two per SM, four stages.  The producer then waits for the preceding
+// grid before its first copy (x may be that grid's output).
+//
+// Requirements: at most 16 tokens, K % 128 == 0 (fp8) / K % 256 == 0 with
 // 16-byte aligned f32 block scales (NF4: the scale tile is a TMA copy; a
 // stage's rows of scales must be whole 16-byte units).  Loading the scales
 // with plain per-thread loads instead measured 19% slower (3072 -> 18432,
@@ -66,10 +72,17 @@ struct SmallM2Cfg {
   static constexpr int kWStageBytes = kBoxes * kBoxBytes;    // 8 KB NF4, 16 KB fp8
   static constexpr int kAbsPerRow = FMT == kFmtNF4 ? 2 * kKgPerStage : 0;  // f32 block scales
   static constexpr int kAStageBytes = kAbsPerRow * 4 * kRows;              // 1 KB NF4
-  static constexpr int kStageBytes = kWStageBytes + kAStageBytes;
+  // Two token tiles (up to 16 tokens): x travels with the stage, as 16-row x
+  // 64-k boxes (128-byte swizzle, rows past M zero-filled), two per k-group
+  static constexpr bool kXStaged = MT == 2;
+  static constexpr int kXBoxBytes = 16 * 128;
+  static constexpr int kXStageBytes = kXStaged ? 2 * kKgPerStage * kXBoxBytes : 0;
+  static constexpr int kOffXInStage = kWStageBytes + kAStageBytes;
+  static constexpr int kStageBytes = kWStageBytes + kAStageBytes + kXStageBytes;
   // CPS resident CTAs per SM: CPS x (smem + 1 KB reserved) <= 228 KB
-  static constexpr int kStages = CPS == 2 ? (FMT == kFmtNF4 ? (MT == 1 ? 8 : 7) : 6)
-                                          : (FMT == kFmtNF4 ? (MT == 1 ? 4 : 3) : 4);
+  static constexpr int kStages = kXStaged ? 4
+                                 : CPS == 2 ? (FMT == kFmtNF4 ? 8 : 6)
+                                            : 4;
   static constexpr int kLutBytes = FMT == kFmtNF4 ? kNf4LutBytes : 0;
   static constexpr int kRedBytes = kConsumerWarps * MT * 128 * 4;
   // offsets from the 1024-byte aligned base (128-byte swizzled boxes)
@@ -81,13 +94,16 @@ struct SmallM2Cfg {
   static constexpr int kSmemBytes = kOffFlag + 16 + 1024;  // + alignment slack
   static_assert(kBoxes >= 1 && kBoxes * kKgPerBox == kKgPerStage, "stage shape");
   static_assert(kStageBytes % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
+  static_assert(kOffXInStage % 1024 == 0, "x boxes keep the 1024-byte swizzle alignment");
+  static_assert(!kXStaged || (R16 == 4 && CPS == 2), "two token tiles: 64-row CTAs, two per SM");
   static_assert(CPS * (kSmemBytes + 1024) <= 228 * 1024, "CPS CTAs per SM");
 };
 
 template <int FMT, int MT, int R16, int CPS>
 __global__ void __launch_bounds__(SmallM2Cfg<FMT, MT, R16, CPS>::kThreads, CPS)
     smallm2_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
-                   const __nv_bfloat16* __restrict__ x, float fp8_scale,
+                   const __grid_constant__ CUtensorMap tmap_x, const __nv_bfloat16* __restrict__ x,
+                   float fp8_scale,
                    const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ y, int M,
                    int N, int K, int act, int64_t ldy) {
   using C = SmallM2Cfg<FMT, MT, R16, CPS>;
@@ -124,6 +140,11 @@ __global__ void __launch_bounds__(SmallM2Cfg<FMT, MT, R16, CPS>::kThreads, CPS)
     if (lane == 0) {
       prefetch_tensormap(&tmap_w);
       if constexpr (FMT == kFmtNF4) prefetch_tensormap(&tmap_a);
+      if constexpr (C::kXStaged) {
+        prefetch_tensormap(&tmap_x);
+        // x may be the output of the kernel before this one on the stream
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+      }
       int s = 0;
       for (; s < S; ++s) {
         const int slot = s % C::kStages;
@@ -137,6 +158,12 @@ __global__ void __launch_bounds__(SmallM2Cfg<FMT, MT, R16, CPS>::kThreads, CPS)
           tma_load_2d(dst + b * C::kBoxBytes, &tmap_w, full_bar(slot), (s * C::kBoxes + b) * 128, row0);
         if constexpr (FMT == kFmtNF4)
           tma_load_2d(dst + C::kWStageBytes, &tmap_a, full_bar(slot), s * C::kAbsPerRow, row0);
+        if constexpr (C::kXStaged) {
+#pragma unroll
+          for (int b = 0; b < 2 * C::kKgPerStage; ++b)
+            tma_load_2d(dst + C::kOffXInStage + b * C::kXBoxBytes, &tmap_x, full_bar(slot),
+                        (s * 2 * C::kKgPerStage + b) * 64, 0);
+        }
       }
       if (*abort_flag) {
         // let issued copies land before shared memory is released (bounded)
@@ -191,6 +218,7 @@ __global__ void __launch_bounds__(SmallM2Cfg<FMT, MT, R16, CPS>::kThreads, CPS)
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
         const int t = 8 * mt + g4;
+        if constexpr (C::kXStaged) break;  // read from the stage below
         if (present && t < M) {
           const uint4* src = reinterpret_cast<const uint4*>(x + t * static_cast<int64_t>(K) + k0);
 #pragma unroll
@@ -206,6 +234,23 @@ __global__ void __launch_bounds__(SmallM2Cfg<FMT, MT, R16, CPS>::kThreads, CPS)
       if (!mbar_wait(full_bar(slot), static_cast<uint32_t>((s / C::kStages) & 1), abort_flag)) break;
       const uint32_t stage = sbase + C::kOffRing + slot * C::kStageBytes;
       const uint32_t box = stage + bx * C::kBoxBytes;
+      if constexpr (C::kXStaged) {
+        // this thread's 32-k run of x (k 128 g + 32 tig ..) for tokens g4 and
+        // 8 + g4: box 2 kgl + tig / 2, bytes 64 (tig % 2) .. of the row, in
+        // 16-byte chunks c at c ^ (row % 8); rows past M arrived as zeros
+        const uint32_t xbox = stage + C::kOffXInStage + (2 * kgl + (tig >> 1)) * C::kXBoxBytes;
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          const int t = 8 * mt + g4;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t ch = static_cast<uint32_t>((4 * (tig & 1) + q) ^ (t & 7)) * 16u;
+            const uint4 v = present ? lds128(xbox + static_cast<uint32_t>(t) * 128u + ch)
+                                    : make_uint4(0u, 0u, 0u, 0u);
+            xw[mt][4 * q] = v.x; xw[mt][4 * q + 1] = v.y; xw[mt][4 * q + 2] = v.z; xw[mt][4 * q + 3] = v.w;
+          }
+        }
+      }
       uint32_t plo[FMT == kFmtNF4 ? 4 : 8], phi[FMT == kFmtNF4 ? 4 : 8];
       uint32_t sc_lo = 0, sc_hi = 0;
       if (present) {

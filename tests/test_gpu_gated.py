@@ -59,6 +59,7 @@ def _close_bitwise(y, ref):
     (4, 256, 0, 300),   # two-phase, separate decode launch
     (1, 0, 3, 16),      # split-K partials + gated reduce
     (5, 0, 0, 4),       # small-M, TMA ring
+    (5, 0, 0, 13),      # small-M, TMA ring, two token tiles (x staged in the ring)
     (6, 0, 0, 12),      # small-M, weights loaded into registers
 ])
 def test_swiglu_epilogue_every_plan(fmt, mode, bm, splits, m):

@@ -173,7 +173,7 @@ def test_small_m_kernel(ops, fmt, m, n, k, with_bias, mode):
     try:
         plan = ops.plan_info(m, n, k, 0 if fmt == "nf4" else 1)
         assert plan["smallm"] and plan["splits"] == 1
-        assert plan["ring"] == (mode == 5 and m <= 8 and k % (256 if fmt == "nf4" else 128) == 0)
+        assert plan["ring"] == (mode == 5 and m <= 16 and k % (256 if fmt == "nf4" else 128) == 0)
         y = _run(ops, fmt, x, w, bias, n)
         y2 = _run(ops, fmt, x, w, bias, n)
         torch.cuda.synchronize()
@@ -186,7 +186,8 @@ def test_small_m_kernel(ops, fmt, m, n, k, with_bias, mode):
 
 @pytest.mark.parametrize("fmt", ["nf4", "fp8"])
 @pytest.mark.parametrize("m,n,k", [(1, 18432, 3072), (8, 3072, 3072), (4, 9216, 3072),
-                                   (1, 12288, 4096), (3, 1000, 15360), (2, 200, 256)])
+                                   (1, 12288, 4096), (3, 1000, 15360), (2, 200, 256),
+                                   (16, 18432, 3072), (12, 3072, 4096), (9, 1000, 15360)])
 def test_small_m_ring_and_register_kernels_agree(ops, fmt, m, n, k):
     # the two small-M kernels decode the same weights into the same MMA
     # fragments in the same k order; the ring kernel alternates two
@@ -363,6 +364,9 @@ def test_plan_choice(ops):
     assert ops.plan_info(4, 3072, 3200, 1)["ring"]
     assert not ops.plan_info(8, 18432, 3072)["ring"]  # from 5 tokens: register-stream kernel
     assert ops.plan_info(16, 18432, 3072)["smallm"]
+    # two token tiles take the ring kernel where its 64-row grid fills the SMs
+    assert ops.plan_info(16, 18432, 3072)["ring"] and ops.plan_info(12, 12288, 4096)["ring"]
+    assert not ops.plan_info(16, 9216, 3072)["ring"]
     small = ops.plan_info(16, 3072, 3072)
     assert not small["smallm"] and not small["pair"] and small["bm"] == 16 and small["splits"] > 1
     assert not ops.plan_info(4, 3072, 3008)["smallm"]  # K % 128 != 0: fused kernel

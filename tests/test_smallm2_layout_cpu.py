@@ -27,11 +27,17 @@ def cfg(fmt, mt, r16, cps=2):
     c["w_stage"] = c["boxes"] * c["box_bytes"]
     c["abs_per_row"] = 2 * c["kg_per_stage"] if fmt == "nf4" else 0
     c["a_stage"] = c["abs_per_row"] * 4 * c["rows"]
-    c["stage"] = c["w_stage"] + c["a_stage"]
-    if cps == 2:
-        c["stages"] = (8 if mt == 1 else 7) if fmt == "nf4" else 6
+    # two token tiles: x staged as 16-row x 64-k boxes, two per k-group
+    c["x_box"] = 16 * 128
+    c["x_stage"] = 2 * c["kg_per_stage"] * c["x_box"] if mt == 2 else 0
+    c["off_x"] = c["w_stage"] + c["a_stage"]
+    c["stage"] = c["w_stage"] + c["a_stage"] + c["x_stage"]
+    if mt == 2:
+        c["stages"] = 4
+    elif cps == 2:
+        c["stages"] = 8 if fmt == "nf4" else 6
     else:
-        c["stages"] = (4 if mt == 1 else 3) if fmt == "nf4" else 4
+        c["stages"] = 4
     c["lut"] = 256 * 32 * 4 if fmt == "nf4" else 0
     c["red"] = 8 * mt * 128 * 4
     c["off_lut"] = c["stages"] * c["stage"]
@@ -68,7 +74,10 @@ def tma_box_plain(src, c0, r0, rows, cols):
 @pytest.mark.parametrize("mt", [1, 2])
 @pytest.mark.parametrize("cps", [2, 3])
 def test_smem_regions_fit_the_resident_ctas(fmt, r16, mt, cps):
+    if mt == 2 and (r16, cps) != (4, 2):
+        pytest.skip("two token tiles run 64-row CTAs, two per SM")
     c = cfg(fmt, mt, r16, cps)
+    assert c["off_x"] % 1024 == 0
     assert c["stage"] % 1024 == 0 and c["box_bytes"] % 1024 == 0
     assert c["boxes"] * c["kg_per_box"] == c["kg_per_stage"]
     assert c["off_lut"] + c["lut"] <= c["off_red"] <= c["off_bar"] < c["off_flag"]
@@ -175,3 +184,43 @@ def test_planner_fills_one_wave_on_148_sms():
         r16, cps = smallm2_config(n, 148)
         assert -(-n // (16 * r16)) <= cps * 148
     assert smallm2_config(40000, 148) == (4, 3)  # beyond one wave
+
+
+@pytest.mark.parametrize("fmt", ["nf4", "fp8"])
+@pytest.mark.parametrize("m", [9, 13, 16])
+def test_two_token_tiles_read_x_from_the_stage(fmt, m):
+    """Emulate the x boxes of a stage (TMA 128-byte swizzle, rows past M
+    zero-filled) and read them back with the consumer threads' addresses:
+    thread (g4, tig) of warp w gets x[t, 128 g + 32 tig .. + 31] for tokens
+    t = g4 and 8 + g4, zeros for t >= M."""
+    rng = np.random.default_rng(m)
+    c = cfg(fmt, 2, 4, 2)
+    k = 3 * 128 * c["kg_per_stage"]
+    x = rng.integers(0, 1 << 16, size=(m, k), dtype=np.uint16)
+    xb = x.view(np.uint8).reshape(m, 2 * k)  # bf16 rows as bytes
+    stages = k // (128 * c["kg_per_stage"])
+    for s in range(stages):
+        xs = np.zeros(c["x_stage"], dtype=np.uint8)
+        for b in range(2 * c["kg_per_stage"]):
+            k0 = (s * 2 * c["kg_per_stage"] + b) * 64
+            box = np.zeros(16 * 128, dtype=np.uint8)
+            for r in range(min(m, 16)):
+                for byte in range(128):
+                    box[r * 128 + ((byte // 16) ^ (r % 8)) * 16 + byte % 16] = xb[r, 2 * k0 + byte]
+            xs[b * c["x_box"]:(b + 1) * c["x_box"]] = box
+        for warp in range(8):
+            kgl = warp // 4
+            g = s * c["kg_per_stage"] + kgl
+            for lane in range(32):
+                g4, tig = lane >> 2, lane & 3
+                xbox = (2 * kgl + (tig >> 1)) * c["x_box"]
+                for mt in range(2):
+                    t = 8 * mt + g4
+                    chunks = []
+                    for q in range(4):
+                        off = xbox + t * 128 + ((4 * (tig & 1) + q) ^ (t & 7)) * 16
+                        chunks.append(xs[off:off + 16])
+                    got = np.concatenate(chunks).view(np.uint16)
+                    k_run = 128 * g + 32 * tig
+                    want = x[t, k_run:k_run + 32] if t < m else np.zeros(32, np.uint16)
+                    np.testing.assert_array_equal(got, want)
