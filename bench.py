@@ -68,6 +68,11 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile-kernels", action="store_true",
                     help="flux_dit: add the per-kernel device-time table of three graph replays")
+    ap.add_argument("--probe", choices=["ring16", "qkv_glue"], default=None,
+                    help="run one kernel a few times for an ncu capture and exit (no JSON line): "
+                         "ring16 = the two-token-tile small-M ring kernel, NF4 x[16,3072] . "
+                         "W[18432,3072]^T, 6 calls; qkv_glue = the FLUX q/k/v norm + RoPE glue at "
+                         "4096 + 512 tokens x 24 heads, 4 calls")
     ap.add_argument("--extras", default="fp8,small,ltx,dit",
                     help="default workload: comma list of the sections measured after the "
                          "headline linear (fp8, small, ltx, dit) or 'none'")
@@ -1259,8 +1264,41 @@ def run_dequant(args, world, rank, local):
         dist.destroy_process_group()
 
 
+def run_probe(which: str):
+    """A few launches of one kernel on small inputs, for an ncu capture."""
+    from diffuser_b200 import flux, ops
+    torch.cuda.set_device(0)
+    if which == "ring16":
+        k, n, m = 3072, 18432, 16
+        w = torch.randn(n, k, device="cuda") * 0.02
+        p, a = ops.ltx23_nf4_quantize(w)
+        ws = [(p, a), (p.clone(), a.clone())]
+        x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+        assert ops.plan_info(m, n, k)["ring"]
+        for i in range(6):
+            ops.nf4_linear(x, ws[i % 2][0], ws[i % 2][1], n)
+    else:
+        H, D, S_img, S_txt = 24, 128, 4096, 512
+        hd = H * D
+        img = torch.randn(1, S_img, 3 * hd, device="cuda").to(torch.bfloat16)
+        txt = torch.randn(1, S_txt, 3 * hd, device="cuda").to(torch.bfloat16)
+        pi = [img[..., j * hd:(j + 1) * hd] for j in range(3)]
+        pt = [txt[..., j * hd:(j + 1) * hd] for j in range(3)]
+        w = [torch.ones(D, device="cuda", dtype=torch.bfloat16) for _ in range(4)]
+        ids = torch.cat([torch.zeros(S_txt, 3), flux.prepare_latent_image_ids(64, 64)], dim=0)
+        rope = flux.pos_embed(ids.cuda(), (16, 56, 56))
+        for _ in range(4):
+            flux.qkv_norm_rope(pi, pt, H, (w[0], w[1], None), (w[2], w[3], None), (True, True, False),
+                               rope, 1e-6)
+    torch.cuda.synchronize()
+    print(f"probe {which}: ok, device error {ops.device_error()}")
+
+
 def main():
     args = parse()
+    if args.probe is not None:
+        run_probe(args.probe)
+        return
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         if args.workload in ("tp_fp8", "flux_dit", "small_nf4", "small_fp8", "dequant_nf4", "dequant_fp8"):
